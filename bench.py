@@ -1,0 +1,572 @@
+#!/usr/bin/env python
+"""Decode-attention bench: tokens/s and achieved HBM bandwidth on B200.
+
+Default workload (the config the metric's 1/2/4/8-GPU
+scaling is quoted on): 256 independent sequences per GPU, Hq=32, Hkv=8,
+d=128, per-sequence KV lengths drawn uniformly from [512, 8192] (seed 3),
+stored contiguously per sequence in one pool, fp16 q/K/V from the
+deterministic N(0,1) generator.  One step = the engine's attention-layer step
+for every sequence: append one K/V row at its position and attend over all of
+its rows (one fused launch of the library's decode kernel).  Positions cycle
+over 16 rows so every step attends L_b+1 .. L_b+16 rows (the workload stays at
+config 3's lengths however many steps run).  Sequences shard across GPUs with
+no communication; each GPU runs its own 256-sequence batch (weak scaling).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl nwd|reference]
+                  [--config 3|1|2] [--scaling weak|strong]
+
+``--impl reference`` times the reference's algorithm on the host CPU: the
+reference is WGSL for a browser WebGPU device, which this machine cannot run,
+so its CPU restatement (oracle/, all host threads) stands in for it, on a
+bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = "nemotron-webgpu-decode_b200"
+METRIC = "decode-attn tokens/s + achieved HBM TB/s vs B200 peak, at 1/2/4/8 GPUs"
+HQ, HKV, HD = 32, 8, 128
+POS_CYCLE = 16
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic(name: str):
+    """dram bytes per launch from a committed ncu summary (profiles/<name>.txt), if any."""
+    path = os.path.join(REPO, "profiles", name + ".txt")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_launch"):
+                return float(line.split()[-1])
+    except OSError:
+        pass
+    return None
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi samples (every 200 ms) for one GPU, tagged with host time."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+    def __init__(self, gpu_id: str):
+        self.rows = []
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", gpu_id, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 8:
+                self.rows.append((time.monotonic(), parts))
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self, t0: float, t1: float):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "note": "nvidia-smi unavailable"}
+        inside = [r for t, r in self.rows if t0 <= t <= t1]
+        window = "timed"
+        if len(inside) < 3:
+            inside = [r for _, r in self.rows]
+            window = "ramp+warmup+timed"
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(r[0]) for r in inside if num(r[0]) is not None]
+        mx = [num(r[1]) for r in inside if num(r[1]) is not None]
+        pw = [num(r[2]) for r in inside if num(r[2]) is not None]
+        reasons = set()
+        for r in inside:
+            for name, v in zip(self.NAMES, r[4:8]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(pw) if pw else None,
+                "reasons": sorted(reasons), "samples": len(inside), "window": window}
+
+
+# ------------------------------------------------------------------ setup
+
+def import_pkg():
+    if REPO not in sys.path:
+        sys.path.insert(0, REPO)
+    return importlib.import_module(PKG + ".ops")
+
+
+def import_oracle():
+    p = os.path.join(REPO, "oracle")
+    if p not in sys.path:
+        sys.path.insert(0, p)
+    import oracle
+    oracle.build()
+    return oracle
+
+
+def config3_lengths():
+    return np.random.default_rng(3).integers(512, 8193, 256).astype(np.int64)
+
+
+def rank_lengths(rank, world, scaling):
+    L = config3_lengths()
+    if scaling == "strong":
+        per = len(L) // world
+        return L[rank * per:(rank + 1) * per]
+    return L
+
+
+def seeds_for(rank):
+    return {"k": 3000 + 100 * rank, "v": 3001 + 100 * rank, "q": 3002 + 100 * rank,
+            "kn": 3003 + 100 * rank, "vn": 3004 + 100 * rank}
+
+
+def step_bytes(L_attended):
+    """Algorithmic HBM bytes of one step: K+V rows read, q read + o write, new K/V row read+write."""
+    B = len(L_attended)
+    return float(4096 * np.sum(L_attended) + B * (2 * HQ * HD * 2 + 4 * HKV * HD * 2))
+
+
+class Config3:
+    def __init__(self, ops, torch, rank, world, scaling, dev):
+        self.ops, self.torch = ops, torch
+        self.L = rank_lengths(rank, world, scaling)
+        self.B = len(self.L)
+        self.caps = self.L + POS_CYCLE
+        self.offs = np.concatenate([[0], np.cumsum(self.caps)[:-1]]).astype(np.int64)
+        self.rows = int(self.caps.sum())
+        sd = seeds_for(rank)
+        self.seeds = sd
+        f16 = torch.float16
+        self.k_pool = torch.empty(self.rows, HKV, HD, dtype=f16, device=dev)
+        self.v_pool = torch.empty_like(self.k_pool)
+        ops.fill_normal(self.k_pool, sd["k"])
+        ops.fill_normal(self.v_pool, sd["v"])
+        self.q = ops.fill_normal(torch.empty(self.B, HQ, HD, dtype=f16, device=dev), sd["q"])
+        self.kn = ops.fill_normal(torch.empty(self.B, HKV, HD, dtype=f16, device=dev), sd["kn"])
+        self.vn = ops.fill_normal(torch.empty(self.B, HKV, HD, dtype=f16, device=dev), sd["vn"])
+        self.o = torch.empty(self.B, HQ, HD, dtype=f16, device=dev)
+        self.row_offset = torch.tensor(self.offs, device=dev)
+        pos = np.stack([self.L + j for j in range(POS_CYCLE)]).astype(np.int32)  # [cycle, B]
+        self.pos_host = pos
+        self.pos = torch.tensor(pos, device=dev)
+        self.ws = ops.Workspace(self.B, HQ, HKV, HD, dev)
+
+    def step(self, s, q=None, kn=None, vn=None, pos=None, o=None):
+        self.ops.kv_append_attention_batched(
+            self.q if q is None else q, self.kn if kn is None else kn,
+            self.vn if vn is None else vn, self.k_pool, self.v_pool, self.row_offset,
+            self.pos[s % POS_CYCLE] if pos is None else pos, self.o if o is None else o,
+            HQ, HKV, HD, workspace=self.ws)
+
+    def bytes_for(self, s):
+        return step_bytes(self.pos_host[s % POS_CYCLE] + 1)
+
+
+# ------------------------------------------------------------------ CPU legs
+
+def cpu_sample(oracle, L, offs_unused, seeds, nseq):
+    """Host copies of the first `nseq` sequences' K/V (same generator streams as the GPU pool)."""
+    caps = L + POS_CYCLE
+    offs = np.concatenate([[0], np.cumsum(caps)[:-1]]).astype(np.int64)
+    sel = list(range(nseq))
+    rows = int(sum(caps[b] for b in sel))
+    k = np.empty((rows, HKV, HD), np.uint16)
+    v = np.empty((rows, HKV, HD), np.uint16)
+    loc = np.zeros(nseq, np.int64)
+    r = 0
+    for i, b in enumerate(sel):
+        n = int(caps[b]) * HKV * HD
+        k[r:r + caps[b]] = oracle.normal_f16(n, seeds["k"], int(offs[b]) * HKV * HD).reshape(-1, HKV, HD)
+        v[r:r + caps[b]] = oracle.normal_f16(n, seeds["v"], int(offs[b]) * HKV * HD).reshape(-1, HKV, HD)
+        loc[i] = r
+        r += int(caps[b])
+    q = oracle.normal_f16(nseq * HQ * HD, seeds["q"])
+    kn = oracle.normal_f16(nseq * HKV * HD, seeds["kn"]).reshape(nseq, HKV * HD)
+    vn = oracle.normal_f16(nseq * HKV * HD, seeds["vn"]).reshape(nseq, HKV * HD)
+    return k, v, loc, q, kn, vn
+
+
+def cpu_step(oracle, L, sample, s):
+    """The reference's step on the CPU for the sample: kv_append K and V at the
+    sequence's position (kv_append.wgsl), then attention over pos+1 rows (sparse_attn.wgsl)."""
+    k, v, loc, q, kn, vn = sample
+    n = len(loc)
+    pos = (L[:n] + (s % POS_CYCLE)).astype(np.int64)
+    for i in range(n):
+        row = loc[i] + pos[i]
+        k[row] = kn[i].reshape(HKV, HD)
+        v[row] = vn[i].reshape(HKV, HD)
+    return oracle.attention_batched(q, k, v, loc, (pos + 1).astype(np.int32), HQ, HKV, HD)
+
+
+def cpu_baseline(oracle, L, seeds, seconds=10.0, nseq=8):
+    sample = cpu_sample(oracle, L, None, seeds, nseq)
+    cpu_step(oracle, L, sample, 0)  # warm
+    t0 = time.perf_counter()
+    steps = 0
+    while True:
+        cpu_step(oracle, L, sample, steps)
+        steps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or steps >= 10000:
+            break
+    return {"value": nseq * steps / el, "unit": "tokens/s", "cores": oracle.num_threads(),
+            "kind": "port",
+            "sample": f"first {nseq} of the 256 config-3 sequences (L={list(map(int, L[:nseq]))}), "
+                      f"{steps} steps of kv_append + attention in {el:.1f} s"}
+
+
+def run_reference(args):
+    """--impl reference: the reference algorithm (oracle port) on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    oracle = import_oracle()
+    L = config3_lengths()
+    seeds = seeds_for(0)
+    nseq = 16
+    sample = cpu_sample(oracle, L, None, seeds, nseq)
+    for s in range(args.warmup):
+        cpu_step(oracle, L, sample, s)
+    t0 = time.perf_counter()
+    for s in range(args.steps):
+        cpu_step(oracle, L, sample, args.warmup + s)
+    el = time.perf_counter() - t0
+    value = nseq * args.steps / el
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": "config3-batched-ragged-decode (sample)", "heads": HQ,
+                   "kv_heads": HKV, "head_dim": HD, "sample_sequences": nseq,
+                   "lengths": list(map(int, L[:nseq]))},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": oracle.num_threads(),
+                         "kind": "port",
+                         "sample": f"{nseq} of 256 sequences per step; the reference's WGSL needs a "
+                                   "browser WebGPU device (unavailable on this box), so its CPU "
+                                   "restatement in oracle/ is timed"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ GPU arm
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=30)
+    ap.add_argument("--impl", choices=["nwd", "reference"], default="nwd")
+    ap.add_argument("--config", choices=["3", "1", "2"], default="3")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--ramp-seconds", type=float, default=1.0)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        if world == 1 and args.gpus > 1:
+            print("run N>1 under torchrun (one process per GPU)", file=sys.stderr)
+            return 2
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    ops = import_pkg()
+    if args.config != "3":
+        return run_small_configs(args, ops, torch, dev, rank, world)
+
+    W = Config3(ops, torch, rank, world, args.scaling, dev)
+    torch.cuda.synchronize()
+    props = torch.cuda.get_device_properties(dev)
+    sampler = ClockSampler("GPU-" + str(props.uuid) if not str(props.uuid).startswith("GPU-")
+                           else str(props.uuid)) if rank == 0 else None
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # clock ramp (untimed), then W warm-up steps, then K timed steps
+    s = 0
+    t_ramp = time.perf_counter()
+    while time.perf_counter() - t_ramp < args.ramp_seconds:
+        for _ in range(20):
+            W.step(s)
+            s += 1
+        torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        W.step(s)
+        s += 1
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.monotonic()
+    start.record()
+    s_first = s
+    for _ in range(args.steps):
+        W.step(s)
+        s += 1
+    end.record()
+    end.synchronize()
+    t1 = time.monotonic()
+    barrier()
+    ms = start.elapsed_time(end)
+    step_bytes_timed = [W.bytes_for(x) for x in range(s_first, s)]
+
+    # roofline pass: per-launch events around the decode kernel (same stream)
+    R = min(args.steps, 50)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(R)]
+    rb = []
+    for i in range(R):
+        evs[i][0].record()
+        W.step(s)
+        evs[i][1].record()
+        rb.append(W.bytes_for(s))
+        s += 1
+    torch.cuda.synchronize()
+    launch_ms = [a.elapsed_time(b) for a, b in evs]
+    kern_ms = statistics.mean(launch_ms)
+    kern_gbs = statistics.mean(rb) / (kern_ms * 1e-3) / 1e9
+
+    # e2e: host buffers through the public API, H2D inputs + D2H output every step
+    e2e = None
+    if not args.no_e2e:
+        pin = dict(pin_memory=True)
+        q_h = W.q.cpu().pin_memory()
+        kn_h = W.kn.cpu().pin_memory()
+        vn_h = W.vn.cpu().pin_memory()
+        pos_h = torch.tensor(W.pos_host).pin_memory()
+        o_h = torch.empty(W.B, HQ, HD, dtype=torch.float16, **pin)
+        q_d, kn_d, vn_d = torch.empty_like(W.q), torch.empty_like(W.kn), torch.empty_like(W.vn)
+        pos_d = torch.empty(W.B, dtype=torch.int32, device=dev)
+        o_d = torch.empty_like(W.o)
+        stream = torch.cuda.current_stream()
+
+        def e2e_step(x):
+            q_d.copy_(q_h, non_blocking=True)
+            kn_d.copy_(kn_h, non_blocking=True)
+            vn_d.copy_(vn_h, non_blocking=True)
+            pos_d.copy_(pos_h[x % POS_CYCLE], non_blocking=True)
+            W.step(x, q=q_d, kn=kn_d, vn=vn_d, pos=pos_d, o=o_d)
+            o_h.copy_(o_d, non_blocking=True)
+            stream.synchronize()
+            return float(o_h[0, 0, 0])  # the host reads the step's result
+
+        for _ in range(args.warmup):
+            e2e_step(s)
+            s += 1
+        barrier()
+        es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        es.record()
+        for _ in range(args.steps):
+            e2e_step(s)
+            s += 1
+        ee.record()
+        ee.synchronize()
+        barrier()
+        e2e_ms = es.elapsed_time(ee)
+        h2d = W.B * (HQ * HD * 2 + 2 * HKV * HD * 2 + 4)
+        d2h = W.B * HQ * HD * 2
+        e2e = {"ms": e2e_ms, "h2d": h2d, "d2h": d2h}
+
+    err = W.ws.check()
+    if err:
+        print(f"device error word {err} after the bench", file=sys.stderr)
+        return 3
+
+    # max over ranks
+    vals_t = torch.tensor([ms, e2e["ms"] if e2e else 0.0], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals_t, op=dist.ReduceOp.MAX)
+    ms_max, e2e_ms_max = float(vals_t[0]), float(vals_t[1])
+    if sampler:
+        sampler.stop()
+    if rank == 0:
+        tokens = W.B * world * args.steps
+        value = tokens / (ms_max * 1e-3)
+        total_bytes = sum(step_bytes_timed) * world
+        peak, peak_kind = peaks()
+        clocks = sampler.summary(t0, t1) if sampler else None
+        traffic = profiled_traffic("decode_kernel_config3_traffic")
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak" if args.scaling == "weak" else "strong",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "hbm_tbs": total_bytes / (ms_max * 1e-3) / 1e12,
+            "config": {
+                "workload": "config3-batched-ragged-decode", "sequences_per_gpu": W.B,
+                "global_batch": W.B * world, "heads": HQ, "kv_heads": HKV, "head_dim": HD,
+                "kv_len": "U[512,8192] seed 3 (+1..16 cycling append rows)",
+                "accumulate": "f32", "step": "fused kv_append + decode attention, 1 launch",
+                "l2": "inputs larger than L2 (~4.6 GB of K/V per step per GPU)",
+                "parallelism": f"sequence-sharded x{world}, no communication"},
+            "roofline": {"bound": "hbm", "achieved": kern_gbs, "peak": peak, "unit": "GB/s",
+                         "frac": kern_gbs / peak, "traffic": traffic,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                         "kernel": "decode_kernel", "launch_ms": kern_ms,
+                         "algorithmic_bytes_per_launch": statistics.mean(rb)},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+        }
+        if e2e:
+            line["e2e"] = {"value": W.B * world * args.steps / (e2e_ms_max * 1e-3),
+                           "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"] * world,
+                           "d2h_bytes_per_step": e2e["d2h"] * world,
+                           "ms_per_step": e2e_ms_max / args.steps,
+                           "path": "ops.kv_append_attention_batched (ctypes -> libnwd.so C ABI), "
+                                   "pinned host buffers, per-step stream sync"}
+        if world == 1 and not args.no_cpu_baseline:
+            oracle = import_oracle()
+            line["cpu_baseline"] = cpu_baseline(oracle, W.L, W.seeds, seconds=args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_small_configs(args, ops, torch, dev, rank, world):
+    """Secondary lines: config 1 (engine trace) and config 2 (L sweep), Hq=40 (engine/config.js)."""
+    if rank != 0:
+        return 0
+    engine = importlib.import_module(PKG + ".engine")
+    peak, _ = peaks()
+    nh = 40
+    out = []
+    if args.config == "1":
+        layer = engine.DecodeAttention(nh, HKV, HD, 256)
+        ops.fill_normal(layer.k_cache, 11)
+        ops.fill_normal(layer.v_cache, 12)
+        q = ops.fill_normal(torch.empty(nh, HD, dtype=torch.float16, device=dev), 13)
+        kn = ops.fill_normal(torch.empty(HKV, HD, dtype=torch.float16, device=dev), 14)
+        o = torch.empty(nh, HD, dtype=torch.float16, device=dev)
+        trace = list(range(151))  # seq 0..150: 24 prompt + 127 decode steps
+
+        def run(n):
+            nbytes = 0.0
+            for i in range(n):
+                layer.seq = trace[i % 151]
+                nbytes += 4096 * (layer.seq + 1) + 2 * nh * HD * 2 + 4 * HKV * HD * 2
+                layer.step(q, kn, kn, out=o)
+            return nbytes
+        run(args.warmup)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        nbytes = run(args.steps)
+        b.record()
+        b.synchronize()
+        ms = a.elapsed_time(b)
+        out.append({"metric": METRIC, "value": args.steps / (ms * 1e-3), "unit": "tokens/s",
+                    "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                    "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+                    "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+                    "hbm_tbs": nbytes / (ms * 1e-3) / 1e12,
+                    "config": {"workload": "config1-engine-trace", "heads": nh, "kv_heads": HKV,
+                               "head_dim": HD, "kv_len": "1..151 (24 prompt + 127 decode)",
+                               "launches_per_step": 1},
+                    "roofline": {"bound": "hbm", "achieved": nbytes / (ms * 1e-3) / 1e9,
+                                 "peak": peak, "unit": "GB/s",
+                                 "frac": nbytes / (ms * 1e-3) / 1e9 / peak}})
+    else:
+        for L in (1024, 4096, 16384, 32768):
+            cap = L + POS_CYCLE
+            layer = engine.DecodeAttention(nh, HKV, HD, cap)
+            ops.fill_normal(layer.k_cache, 21)
+            ops.fill_normal(layer.v_cache, 22)
+            q = ops.fill_normal(torch.empty(nh, HD, dtype=torch.float16, device=dev), 23)
+            kn = ops.fill_normal(torch.empty(HKV, HD, dtype=torch.float16, device=dev), 24)
+            o = torch.empty(nh, HD, dtype=torch.float16, device=dev)
+
+            def run(n):
+                nbytes = 0.0
+                for i in range(n):
+                    layer.seq = L - 1 + (i % POS_CYCLE)
+                    nbytes += 4096 * (layer.seq + 1) + 2 * nh * HD * 2 + 4 * HKV * HD * 2
+                    layer.step(q, kn, kn, out=o)
+                return nbytes
+            run(args.warmup)
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            nbytes = run(args.steps)
+            b.record()
+            b.synchronize()
+            ms = a.elapsed_time(b)
+            out.append({"metric": METRIC, "value": args.steps / (ms * 1e-3), "unit": "tokens/s",
+                        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                        "ms_per_step": ms / args.steps, "higher_is_better": True,
+                        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+                        "data": "synthetic", "hbm_tbs": nbytes / (ms * 1e-3) / 1e12,
+                        "config": {"workload": f"config2-L{L}", "heads": nh, "kv_heads": HKV,
+                                   "head_dim": HD, "kv_len": L},
+                        "roofline": {"bound": "hbm", "achieved": nbytes / (ms * 1e-3) / 1e9,
+                                     "peak": peak, "unit": "GB/s",
+                                     "frac": nbytes / (ms * 1e-3) / 1e9 / peak}})
+    for line in out:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,191 @@
+/*
+ * nwd.h — C ABI of the B200 (sm_100a) decode-attention engine.
+ *
+ * This library replaces the two WGSL dispatch sites of the Nemotron WebGPU
+ * decode engine's attention layers:
+ *   - kernels/kv_append.wgsl   (KV-cache row write, dispatched at engine/runtime.js:389-390)
+ *   - kernels/sparse_attn.wgsl (GQA decode attention, dispatched at engine/runtime.js:391)
+ * and extends them to ragged batches, long contexts and multi-GPU shards.
+ *
+ * Conventions
+ *   - Every entry point returns an int status: NWD_OK (0) or one of NWD_ERR_*.
+ *     On error nothing is launched and nwd_last_error() returns a message
+ *     (thread-local, valid until the next call on the same thread).  This
+ *     mirrors the reference's throw-on-error style (engine/runtime.js:448,
+ *     kernels/gpu.js:127-131): a JS shim turns a non-zero status into
+ *     `throw new Error(nwd_last_error())`.
+ *   - Tensors are device pointers.  fp16 data are passed as `uint16_t*`
+ *     (IEEE binary16 bit patterns).  Buffers are owned by the caller; the
+ *     library never allocates or frees caller memory.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream).  Calls are stream-ordered and asynchronous.
+ *   - KV caches are token-major, exactly as the reference lays them out
+ *     (kernels/sparse_attn.wgsl:49,107; kernels/kv_append.wgsl:17):
+ *     element (t, h, i) of a cache lives at ((t * n_kv + h) * hd + i).
+ *   - Softmax scale: pass 0.0f for the reference's inverseSqrt(head_dim)
+ *     (kernels/sparse_attn.wgsl:42).
+ *   - The attention kernels support head_dim == 128 and a GQA group
+ *     n_heads / n_kv_heads in 1..8 (the engine uses 40/8 = 5,
+ *     engine/config.js:10-12).  Other shapes return NWD_ERR_UNSUPPORTED.
+ */
+#ifndef NWD_H
+#define NWD_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NWD_OK 0
+#define NWD_ERR_INVALID 1     /* null pointer, zero shape, n_heads % n_kv_heads != 0 */
+#define NWD_ERR_RANGE 2       /* seq >= cache capacity (engine/runtime.js:448) */
+#define NWD_ERR_UNSUPPORTED 3 /* shape outside the kernels' supported set */
+#define NWD_ERR_WORKSPACE 4   /* workspace missing, too small or misaligned */
+#define NWD_ERR_CUDA 5        /* CUDA runtime / driver error */
+#define NWD_ERR_NCCL 6        /* NCCL missing or a collective failed */
+#define NWD_ERR_TIMEOUT 7     /* a bounded device- or host-side wait gave up */
+#define NWD_ERR_DEVICE 8      /* a kernel recorded an error in its workspace */
+
+/* Last error message of the calling thread ("" if none). */
+const char* nwd_last_error(void);
+/* Library version string. */
+const char* nwd_version(void);
+/* Name of a status code. */
+const char* nwd_status_name(int status);
+
+/* ------------------------------------------------------------------ */
+/* KV-cache append                                                     */
+/* ------------------------------------------------------------------ */
+
+/* kernels/kv_append.wgsl:1-18 — cache[seq * n_kv * hd + i] = src[i] for
+ * i < n_kv * hd.  Argument order follows the WGSL Params {seq, n_kv, hd}.
+ * `cap` is the cache capacity in rows (engine/config.js:24 maxSeq); seq >= cap
+ * returns NWD_ERR_RANGE without launching (engine/runtime.js:448). Bit-exact. */
+int nwd_kv_append(const uint16_t* src, uint16_t* cache, uint32_t seq, uint32_t n_kv,
+                  uint32_t hd, uint32_t cap, void* stream);
+
+/* The engine's two kv_append dispatches (K then V, engine/runtime.js:389-390)
+ * as one launch. */
+int nwd_kv_append_kv(const uint16_t* k_src, const uint16_t* v_src, uint16_t* k_cache,
+                     uint16_t* v_cache, uint32_t seq, uint32_t n_kv, uint32_t hd, uint32_t cap,
+                     void* stream);
+
+/* Ragged batch of the same write: sequence b writes its row pos[b] of a
+ * region that starts at pool row row_offset[b].
+ *   k_src, v_src : [batch, n_kv, hd]
+ *   k_pool, v_pool: [pool_rows, n_kv, hd]
+ *   row_offset   : device int64[batch];  pos: device int32[batch]
+ * Rows with row_offset[b] + pos[b] outside [0, pool_rows) are skipped and
+ * counted in the optional device word `*err_count` (may be NULL). */
+int nwd_kv_append_batched(const uint16_t* k_src, const uint16_t* v_src, uint16_t* k_pool,
+                          uint16_t* v_pool, uint64_t pool_rows, const int64_t* row_offset,
+                          const int32_t* pos, uint32_t batch, uint32_t n_kv, uint32_t hd,
+                          uint32_t* err_count, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* Decode attention (split-KV flash-decode)                            */
+/* ------------------------------------------------------------------ */
+
+/* Bytes of workspace the decode calls below need for `batch` sequences on
+ * the current device.  The workspace must be zero-filled once before its
+ * first use (nwd_workspace_init or cudaMemset); every call leaves it ready
+ * for the next.  Its layout follows the call's (batch, n_heads, n_kv_heads,
+ * head_dim): use one workspace per shape, or zero it again before using it
+ * for another.  Calls that share one workspace must not overlap on the GPU.
+ * The base pointer must be 256-byte aligned.  If nwd_workspace_check reports
+ * a device error, zero the workspace before reusing it. */
+int nwd_attn_decode_workspace_size(uint32_t batch, uint32_t n_heads, uint32_t n_kv_heads,
+                                   uint32_t head_dim, size_t* bytes);
+
+/* Zero-fills a workspace on `stream`. */
+int nwd_workspace_init(void* workspace, size_t ws_bytes, void* stream);
+
+/* Reads (synchronously, on `stream`) and clears the device-side error word
+ * of a workspace: 0 = no error, else a NWD_DEVERR_* code. */
+int nwd_workspace_check(void* workspace, size_t ws_bytes, uint32_t* device_error,
+                        void* stream);
+
+#define NWD_DEVERR_PIPE_TIMEOUT 1u  /* an mbarrier wait hit its iteration limit */
+#define NWD_DEVERR_ROW_RANGE 2u     /* a row index fell outside the pool */
+
+/* kernels/sparse_attn.wgsl:32-113 — for each query head h:
+ *   O[h,:] = softmax(scale * Q[h,:] . K[t, h/group, :]^T, t < seq) . V[t, h/group, :]
+ * The first four scalars are the WGSL Params {n_heads, n_kv_heads, head_dim,
+ * seq} (kernels/sparse_attn.wgsl:12-17); `seq` is the number of cached rows
+ * attended (the engine passes this.seq + 1, engine/runtime.js:452).
+ *   q: [n_heads, head_dim]   k_cache, v_cache: [cap, n_kv_heads, head_dim]
+ *   o: [n_heads, head_dim]   fp16 in, fp32 accumulation, fp16 out.
+ * seq == 0 writes zeros (the WGSL's acc stays 0). */
+int nwd_attn_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                    uint16_t* o, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
+                    uint32_t seq, uint32_t cap, float scale, void* workspace, size_t ws_bytes,
+                    void* stream);
+
+/* One engine attention step (engine/runtime.js:389-391 with the uniforms of
+ * :451-452): writes k_new/v_new ([n_kv_heads, head_dim]) into row `seq` of the
+ * caches, then attends over rows 0..seq (seq + 1 rows), in one launch. */
+int nwd_kv_append_attn_decode(const uint16_t* q, const uint16_t* k_new, const uint16_t* v_new,
+                              uint16_t* k_cache, uint16_t* v_cache, uint16_t* o,
+                              uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
+                              uint32_t seq, uint32_t cap, float scale, void* workspace,
+                              size_t ws_bytes, void* stream);
+
+/* Ragged batch of independent sequences sharing one KV pool.
+ *   q, o        : [batch, n_heads, head_dim]
+ *   k_pool, v_pool: [pool_rows, n_kv_heads, head_dim]
+ *   row_offset  : device int64[batch] — first pool row of sequence b
+ *   seq_len     : device int32[batch] — rows attended for sequence b
+ * batch <= 4096 per call. */
+int nwd_attn_decode_batched(const uint16_t* q, const uint16_t* k_pool, const uint16_t* v_pool,
+                            uint64_t pool_rows, const int64_t* row_offset,
+                            const int32_t* seq_len, uint16_t* o, uint32_t batch,
+                            uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
+                            float scale, void* workspace, size_t ws_bytes, void* stream);
+
+/* Batched engine step: sequence b writes k_new/v_new[b] into its row pos[b],
+ * then attends over pos[b] + 1 rows.  One launch. */
+int nwd_kv_append_attn_decode_batched(const uint16_t* q, const uint16_t* k_new,
+                                      const uint16_t* v_new, uint16_t* k_pool, uint16_t* v_pool,
+                                      uint64_t pool_rows, const int64_t* row_offset,
+                                      const int32_t* pos, uint16_t* o, uint32_t batch,
+                                      uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
+                                      float scale, void* workspace, size_t ws_bytes,
+                                      void* stream);
+
+/* Partial attention over a shard of each sequence's rows, for merging across
+ * shards (GPUs).  Same inputs as nwd_attn_decode_batched; instead of O it
+ * writes, per (b, h):
+ *   part_ml[(b*n_heads+h)*2 + 0] = m = max_t s_t * log2(e)   (log2 units)
+ *   part_ml[(b*n_heads+h)*2 + 1] = l = sum_t 2^(s_t*log2(e) - m)
+ *   part_o [(b*n_heads+h)*head_dim + i] = sum_t 2^(s_t*log2(e) - m) * V[t,i]
+ * with s_t = scale * q.k_t.  An empty shard writes m = -inf, l = 0, o = 0. */
+int nwd_attn_decode_partial(const uint16_t* q, const uint16_t* k_pool, const uint16_t* v_pool,
+                            uint64_t pool_rows, const int64_t* row_offset,
+                            const int32_t* seq_len, float* part_o, float* part_ml,
+                            uint32_t batch, uint32_t n_heads, uint32_t n_kv_heads,
+                            uint32_t head_dim, float scale, void* workspace, size_t ws_bytes,
+                            void* stream);
+
+/* Log-sum-exp merge of `shards` partials laid out [shards][batch*n_heads][...]
+ * (as nwd_attn_decode_partial writes them) into o [batch, n_heads, head_dim]
+ * fp16.  Shards are merged in index order. */
+int nwd_attn_merge(const float* part_o, const float* part_ml, uint16_t* o, uint32_t shards,
+                   uint32_t batch, uint32_t n_heads, uint32_t head_dim, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* Synthetic inputs                                                    */
+/* ------------------------------------------------------------------ */
+
+/* Fills dst[0..n) with the deterministic fp16 N(0,1) stream element
+ * offset+i of `seed` (Irwin-Hall sum of 12 16-bit uniforms from splitmix64,
+ * integer-exact, bit-identical to the CPU oracle's generator). */
+int nwd_fill_normal_f16(uint16_t* dst, uint64_t n, uint64_t seed, uint64_t offset,
+                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NWD_H */

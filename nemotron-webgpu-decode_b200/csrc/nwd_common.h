@@ -1,0 +1,56 @@
+// Internal host/device helpers shared by the library's translation units.
+#pragma once
+
+#include <cuda.h>  // CUtensorMap and enums only; the driver is reached via cudaGetDriverEntryPoint
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "nwd.h"
+
+namespace nwd {
+
+// ---- error reporting (thread-local last error) ----
+int fail(int status, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int cuda_fail(cudaError_t e, const char* what);
+int ok();  // clears the last error, returns NWD_OK
+
+// ---- per-device facts ----
+struct DeviceInfo {
+  int device = -1;
+  int sm_count = 0;
+  int major = 0, minor = 0;
+  size_t smem_optin = 0;
+};
+int current_device_info(DeviceInfo* out);
+
+// ---- TMA descriptors ----
+// Encodes (or returns a cached copy of) the 4-D tensor map the decode kernel
+// uses for a token-major cache [rows, n_kv, hd] of fp16:
+//   dims {64, hd/64, n_kv, rows}, box {64, hd/64, 1, box_rows}, 128-byte swizzle.
+int kv_tensor_map(CUtensorMap* out, const void* base, uint64_t rows, uint32_t n_kv, uint32_t hd,
+                  uint32_t box_rows);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---- workspace layout shared by the decode kernels ----
+// [0, 256)            header: error word, scheduler counters
+// [256, +tickets)     uint32 per (sequence, kv head) merge tickets
+// then                float2 (m, l) per (unit, head) and float[hd] per (unit, head)
+struct WsHeader {
+  uint32_t error;       // NWD_DEVERR_* bits
+  uint32_t next_unit;   // dynamic scheduler: next unit to hand out
+  uint32_t done_ctas;   // CTAs that found the queue empty
+  uint32_t pad[61];
+};
+static_assert(sizeof(WsHeader) == 256, "header is 256 bytes");
+
+struct WsLayout {
+  size_t tickets_off, ml_off, o_off, total;
+  uint32_t max_units;
+};
+// Layout for `batch` sequences, kv heads n_kv, group g, on a device with
+// `units_cap` units at most (see decode.cu for the chunk policy).
+WsLayout ws_layout(uint32_t batch, uint32_t n_kv, uint32_t group, uint32_t hd, uint32_t units_cap);
+
+}  // namespace nwd

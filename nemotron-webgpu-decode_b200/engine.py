@@ -1,0 +1,105 @@
+"""Attention-layer state of the reference's DecodeEngine, on the B200 library.
+
+``engine/runtime.js`` keeps, per attention layer, two f32 caches of
+``maxSeq * kvHeads * headDim`` (runtime.js:170-173), a step counter ``seq``
+(runtime.js:66, :467) and two uniforms rewritten every step
+(``uKv[0] = seq``, ``uAttn[3] = seq + 1``, runtime.js:451-452).  Each step
+dispatches kv_append(K), kv_append(V) and attention (runtime.js:389-391) and
+throws once ``seq`` reaches ``maxSeq`` (runtime.js:448).  ``reset()`` wipes the
+caches (runtime.js:615-633).
+
+:class:`DecodeAttention` is that slice for one layer, with fp16 caches and the
+three dispatches fused into one launch; :class:`BatchedDecodeAttention` is
+the same for a ragged batch of independent sequences sharing one KV pool.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import ops
+from ._lib import NWD_ERR_RANGE, NwdError
+
+# engine/config.js:10-12, :24
+NANO4B_HEADS = 40
+NANO4B_KV_HEADS = 8
+NANO4B_HEAD_DIM = 128
+NANO4B_MAX_SEQ = 256
+
+
+class DecodeAttention:
+    """One attention layer's KV cache + step (runtime.js:170-173, :389-391, :447-467)."""
+
+    def __init__(self, heads: int = NANO4B_HEADS, kv_heads: int = NANO4B_KV_HEADS,
+                 head_dim: int = NANO4B_HEAD_DIM, max_seq: int = NANO4B_MAX_SEQ,
+                 device="cuda", scale: float = 0.0):
+        self.heads, self.kv_heads, self.head_dim, self.max_seq = heads, kv_heads, head_dim, max_seq
+        self.device = torch.device(device)
+        self.scale = scale
+        self.k_cache = torch.zeros(max_seq, kv_heads, head_dim, dtype=torch.float16,
+                                   device=self.device)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        self.workspace = ops.Workspace(1, heads, kv_heads, head_dim, self.device)
+        self.seq = 0
+
+    def step(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+             out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """Append this token's k/v at row ``seq`` and attend over ``seq + 1`` rows."""
+        if self.seq >= self.max_seq:
+            raise NwdError(NWD_ERR_RANGE, f"seq {self.seq} exceeds maxSeq {self.max_seq}")
+        if out is None:
+            out = torch.empty(self.heads, self.head_dim, dtype=torch.float16, device=self.device)
+        params = ops.AttnParams(self.heads, self.kv_heads, self.head_dim, self.seq)
+        ops.kv_append_attention(q, k, v, self.k_cache, self.v_cache, out, params,
+                                scale=self.scale, workspace=self.workspace, stream=stream)
+        self.seq += 1
+        return out
+
+    def reset(self) -> None:
+        """runtime.js:615-633: seq = 0 and the caches wiped."""
+        self.seq = 0
+        self.k_cache.zero_()
+        self.v_cache.zero_()
+
+
+class BatchedDecodeAttention:
+    """Ragged batch of sequences in one pool: sequence b owns pool rows
+    [row_offset[b], row_offset[b] + capacity[b]) and has ``lengths[b]`` rows."""
+
+    def __init__(self, capacities, heads: int, kv_heads: int, head_dim: int = 128,
+                 device="cuda", scale: float = 0.0):
+        self.device = torch.device(device)
+        caps = torch.as_tensor(list(capacities), dtype=torch.int64)
+        self.batch = int(caps.numel())
+        offs = torch.zeros_like(caps)
+        if self.batch > 1:
+            offs[1:] = torch.cumsum(caps, 0)[:-1]
+        self.capacity = caps
+        self.pool_rows = int(caps.sum())
+        self.heads, self.kv_heads, self.head_dim = heads, kv_heads, head_dim
+        self.scale = scale
+        self.k_pool = torch.zeros(self.pool_rows, kv_heads, head_dim, dtype=torch.float16,
+                                  device=self.device)
+        self.v_pool = torch.zeros_like(self.k_pool)
+        self.row_offset = offs.to(self.device)
+        self.lengths = torch.zeros(self.batch, dtype=torch.int32, device=self.device)
+        self.workspace = ops.Workspace(self.batch, heads, kv_heads, head_dim, self.device)
+
+    def step(self, q, k_new, v_new, out=None, stream=None) -> torch.Tensor:
+        """Every sequence appends one row and attends over its rows (fused launch)."""
+        if out is None:
+            out = torch.empty(self.batch, self.heads, self.head_dim, dtype=torch.float16,
+                              device=self.device)
+        ops.kv_append_attention_batched(q, k_new, v_new, self.k_pool, self.v_pool,
+                                        self.row_offset, self.lengths, out, self.heads,
+                                        self.kv_heads, self.head_dim, scale=self.scale,
+                                        workspace=self.workspace, stream=stream)
+        self.lengths += 1
+        return out
+
+    def attend(self, q, out=None, stream=None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty(self.batch, self.heads, self.head_dim, dtype=torch.float16,
+                              device=self.device)
+        return ops.attention_batched(q, self.k_pool, self.v_pool, self.row_offset, self.lengths,
+                                     out, self.heads, self.kv_heads, self.head_dim,
+                                     scale=self.scale, workspace=self.workspace, stream=stream)

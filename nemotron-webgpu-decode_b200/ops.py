@@ -1,0 +1,251 @@
+"""Operator API of the decode-attention path, over torch CUDA tensors.
+
+The names and argument meaning follow the reference's two WGSL kernels:
+
+* ``kv_append(src, cache, KvParams(seq, n_kv, hd))`` — kernels/kv_append.wgsl
+  (uniform ``Params{seq, n_kv, hd}``, kernels/kv_append.wgsl:1-6);
+* ``attention(q, k_cache, v_cache, o, AttnParams(n_heads, n_kv_heads,
+  head_dim, seq))`` — kernels/sparse_attn.wgsl (uniform ``Params{n_heads,
+  n_kv_heads, head_dim, seq}``, kernels/sparse_attn.wgsl:12-17).
+
+Differences from the WGSL, all intentional: fp16 storage with fp32
+accumulation (the WGSL buffers are f32), no 256-row cap, an optional softmax
+``scale`` (0 keeps the reference's inverseSqrt(head_dim)), a caller-visible
+workspace for the split-KV partials, and ragged-batch / shard-partial
+variants.  Errors raise :class:`NwdError` with the library's message, as the
+reference throws ``Error`` (engine/runtime.js:448).
+
+torch is used only to hold device memory and to name the current stream; all
+computation runs in ``libnwd.so``.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import NwdError, call
+
+
+@dataclass
+class KvParams:
+    """kernels/kv_append.wgsl:1-6 ``Params{seq, n_kv, hd}``."""
+    seq: int
+    n_kv: int
+    hd: int
+
+
+@dataclass
+class AttnParams:
+    """kernels/sparse_attn.wgsl:12-17 ``Params{n_heads, n_kv_heads, head_dim, seq}``."""
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    seq: int
+
+
+def _stream(stream=None) -> int:
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return int(stream.cuda_stream) if hasattr(stream, "cuda_stream") else int(stream)
+
+
+def _ptr(t: torch.Tensor, dtype, name: str) -> int:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t.data_ptr()
+
+
+def _h(t, name):
+    return _ptr(t, torch.float16, name)
+
+
+class Workspace:
+    """Device scratch for the split-KV partials and the work queue.
+
+    Sized for ``batch`` sequences of the given head shape on the current
+    device and zero-filled once; calls leave it ready for the next call.
+    Calls sharing one workspace must be ordered on one stream.
+    """
+
+    def __init__(self, batch: int, n_heads: int, n_kv_heads: int, head_dim: int,
+                 device=None):
+        lib = _lib.load()
+        nbytes = ctypes.c_size_t(0)
+        device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        with torch.cuda.device(device):
+            _lib.check(lib.nwd_attn_decode_workspace_size(batch, n_heads, n_kv_heads, head_dim,
+                                                          ctypes.byref(nbytes)))
+            self.nbytes = int(nbytes.value)
+            # +256 so the base can be rounded up to a 256-byte boundary
+            self._buf = torch.zeros(self.nbytes + 256, dtype=torch.uint8, device=device)
+        base = self._buf.data_ptr()
+        self.ptr = (base + 255) // 256 * 256
+        self.shape = (batch, n_heads, n_kv_heads, head_dim)
+        self.device = device
+
+    def fits(self, batch: int, n_heads: int, n_kv_heads: int, head_dim: int) -> bool:
+        # the library derives the workspace layout from the call's shape, so a
+        # workspace serves exactly the shape it was sized (and zeroed) for
+        return self.shape == (batch, n_heads, n_kv_heads, head_dim)
+
+    def check(self, stream=None) -> int:
+        """Synchronously read and clear the device-side error word (0 = ok)."""
+        v = ctypes.c_uint32(0)
+        call("nwd_workspace_check", self.ptr, self.nbytes, ctypes.byref(v), _stream(stream))
+        return int(v.value)
+
+
+_ws_cache: dict = {}
+
+
+def _workspace(batch, n_heads, n_kv, hd, device, ws):
+    if ws is not None:
+        return ws
+    key = (device.index if device.index is not None else torch.cuda.current_device(),
+           batch, n_heads, n_kv, hd)
+    cur = _ws_cache.get(key)
+    if cur is None:
+        cur = Workspace(batch, n_heads, n_kv, hd, device)
+        _ws_cache[key] = cur
+    return cur
+
+
+# ---------------------------------------------------------------- kv_append
+
+def kv_append(src: torch.Tensor, cache: torch.Tensor, params: KvParams, stream=None) -> None:
+    """Write ``src`` ([n_kv*hd] fp16) into row ``params.seq`` of ``cache``.
+
+    ``cache`` is [max_seq, n_kv, hd] (any shape with max_seq rows of n_kv*hd);
+    ``seq >= max_seq`` raises NwdError (NWD_ERR_RANGE) without launching.
+    """
+    n = params.n_kv * params.hd
+    if src.numel() < n:
+        raise ValueError(f"src has {src.numel()} elements, need {n}")
+    cap = cache.numel() // n
+    call("nwd_kv_append", _h(src, "src"), _h(cache, "cache"), params.seq, params.n_kv, params.hd,
+         cap, _stream(stream))
+
+
+def kv_append_kv(k_src, v_src, k_cache, v_cache, params: KvParams, stream=None) -> None:
+    """Both of the engine's kv_append dispatches (runtime.js:389-390) in one launch."""
+    n = params.n_kv * params.hd
+    cap = k_cache.numel() // n
+    if v_cache.numel() // n != cap:
+        raise ValueError("k_cache and v_cache differ in capacity")
+    call("nwd_kv_append_kv", _h(k_src, "k_src"), _h(v_src, "v_src"), _h(k_cache, "k_cache"),
+         _h(v_cache, "v_cache"), params.seq, params.n_kv, params.hd, cap, _stream(stream))
+
+
+def kv_append_batched(k_src, v_src, k_pool, v_pool, row_offset, pos, err_count=None,
+                      stream=None) -> None:
+    """Sequence b writes k_src[b]/v_src[b] into pool row row_offset[b] + pos[b]."""
+    batch = pos.numel()
+    n_kv, hd = k_src.shape[-2], k_src.shape[-1]
+    rows = k_pool.numel() // (n_kv * hd)
+    ec = _ptr(err_count, torch.int32, "err_count") if err_count is not None else None
+    call("nwd_kv_append_batched", _h(k_src, "k_src"), _h(v_src, "v_src"), _h(k_pool, "k_pool"),
+         _h(v_pool, "v_pool"), rows, _ptr(row_offset, torch.int64, "row_offset"),
+         _ptr(pos, torch.int32, "pos"), batch, n_kv, hd, ec, _stream(stream))
+
+
+# ---------------------------------------------------------------- attention
+
+def attention(q, k_cache, v_cache, o, params: AttnParams, scale: float = 0.0, workspace=None,
+              stream=None) -> torch.Tensor:
+    """One dispatch of kernels/sparse_attn.wgsl: o[h] = softmax(q[h].K^T) V over ``seq`` rows."""
+    n = params.n_kv_heads * params.head_dim
+    cap = k_cache.numel() // n
+    ws = _workspace(1, params.n_heads, params.n_kv_heads, params.head_dim, q.device, workspace)
+    call("nwd_attn_decode", _h(q, "q"), _h(k_cache, "k_cache"), _h(v_cache, "v_cache"),
+         _h(o, "o"), params.n_heads, params.n_kv_heads, params.head_dim, params.seq, cap,
+         float(scale), ws.ptr, ws.nbytes, _stream(stream))
+    return o
+
+
+def kv_append_attention(q, k_new, v_new, k_cache, v_cache, o, params: AttnParams,
+                        scale: float = 0.0, workspace=None, stream=None) -> torch.Tensor:
+    """The engine's attention-layer step (runtime.js:389-391, uniforms of :451-452):
+    write k_new/v_new at row ``params.seq``, then attend over ``params.seq + 1`` rows."""
+    n = params.n_kv_heads * params.head_dim
+    cap = k_cache.numel() // n
+    ws = _workspace(1, params.n_heads, params.n_kv_heads, params.head_dim, q.device, workspace)
+    call("nwd_kv_append_attn_decode", _h(q, "q"), _h(k_new, "k_new"), _h(v_new, "v_new"),
+         _h(k_cache, "k_cache"), _h(v_cache, "v_cache"), _h(o, "o"), params.n_heads,
+         params.n_kv_heads, params.head_dim, params.seq, cap, float(scale), ws.ptr, ws.nbytes,
+         _stream(stream))
+    return o
+
+
+def attention_batched(q, k_pool, v_pool, row_offset, seq_len, o, n_heads, n_kv_heads, head_dim,
+                      scale: float = 0.0, workspace=None, stream=None) -> torch.Tensor:
+    """Ragged batch: q/o [B, n_heads, head_dim]; sequence b attends pool rows
+    [row_offset[b], row_offset[b] + seq_len[b])."""
+    batch = seq_len.numel()
+    rows = k_pool.numel() // (n_kv_heads * head_dim)
+    ws = _workspace(batch, n_heads, n_kv_heads, head_dim, q.device, workspace)
+    call("nwd_attn_decode_batched", _h(q, "q"), _h(k_pool, "k_pool"), _h(v_pool, "v_pool"), rows,
+         _ptr(row_offset, torch.int64, "row_offset"), _ptr(seq_len, torch.int32, "seq_len"),
+         _h(o, "o"), batch, n_heads, n_kv_heads, head_dim, float(scale), ws.ptr, ws.nbytes,
+         _stream(stream))
+    return o
+
+
+def kv_append_attention_batched(q, k_new, v_new, k_pool, v_pool, row_offset, pos, o, n_heads,
+                                n_kv_heads, head_dim, scale: float = 0.0, workspace=None,
+                                stream=None) -> torch.Tensor:
+    """Batched engine step: sequence b writes its new row at pos[b], attends pos[b] + 1 rows."""
+    batch = pos.numel()
+    rows = k_pool.numel() // (n_kv_heads * head_dim)
+    ws = _workspace(batch, n_heads, n_kv_heads, head_dim, q.device, workspace)
+    call("nwd_kv_append_attn_decode_batched", _h(q, "q"), _h(k_new, "k_new"), _h(v_new, "v_new"),
+         _h(k_pool, "k_pool"), _h(v_pool, "v_pool"), rows,
+         _ptr(row_offset, torch.int64, "row_offset"), _ptr(pos, torch.int32, "pos"), _h(o, "o"),
+         batch, n_heads, n_kv_heads, head_dim, float(scale), ws.ptr, ws.nbytes, _stream(stream))
+    return o
+
+
+def attention_partial(q, k_pool, v_pool, row_offset, seq_len, part_o, part_ml, n_heads,
+                      n_kv_heads, head_dim, scale: float = 0.0, workspace=None, stream=None):
+    """Shard partials: part_o [B, n_heads, hd] f32 (unnormalised), part_ml [B, n_heads, 2]
+    f32 = (max in log2 units, sum of 2^(s - max))."""
+    batch = seq_len.numel()
+    rows = k_pool.numel() // (n_kv_heads * head_dim)
+    ws = _workspace(batch, n_heads, n_kv_heads, head_dim, q.device, workspace)
+    call("nwd_attn_decode_partial", _h(q, "q"), _h(k_pool, "k_pool"), _h(v_pool, "v_pool"), rows,
+         _ptr(row_offset, torch.int64, "row_offset"), _ptr(seq_len, torch.int32, "seq_len"),
+         _ptr(part_o, torch.float32, "part_o"), _ptr(part_ml, torch.float32, "part_ml"), batch,
+         n_heads, n_kv_heads, head_dim, float(scale), ws.ptr, ws.nbytes, _stream(stream))
+    return part_o, part_ml
+
+
+def merge(part_o, part_ml, o, stream=None) -> torch.Tensor:
+    """LSE-merge [shards, B, n_heads, hd] partials into o [B, n_heads, hd] fp16."""
+    shards = part_o.shape[0]
+    batch, n_heads, hd = o.shape[-3], o.shape[-2], o.shape[-1]
+    call("nwd_attn_merge", _ptr(part_o, torch.float32, "part_o"),
+         _ptr(part_ml, torch.float32, "part_ml"), _h(o, "o"), shards, batch, n_heads, hd,
+         _stream(stream))
+    return o
+
+
+def fill_normal(t: torch.Tensor, seed: int, offset: int = 0, stream=None) -> torch.Tensor:
+    """Fill an fp16 tensor with the deterministic N(0,1) stream (bit-identical to the CPU
+    generator used by the tests)."""
+    call("nwd_fill_normal_f16", _h(t, "t"), t.numel(), int(seed), int(offset), _stream(stream))
+    return t
+
+
+__all__ = [
+    "KvParams", "AttnParams", "Workspace", "NwdError", "kv_append", "kv_append_kv",
+    "kv_append_batched", "attention", "kv_append_attention", "attention_batched",
+    "kv_append_attention_batched", "attention_partial", "merge", "fill_normal",
+]

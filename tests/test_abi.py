@@ -1,0 +1,82 @@
+"""The C-ABI library loads and exports every symbol include/nwd.h declares.
+
+These checks make no compute call, so they run without a GPU.  Argument
+checks that fail before any CUDA call (range, null pointers) are exercised
+too: they must return their status without launching anything.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+
+
+def test_library_exports_header_symbols(nwd):
+    from importlib import import_module
+    _lib = import_module(nwd.__name__ + "._lib")
+    syms = _lib.header_symbols()
+    assert len(syms) >= 15
+    lib = _lib.load()
+    missing = [s for s in syms if not hasattr(lib, s)]
+    assert not missing, missing
+    # every declared symbol has a ctypes signature, and vice versa
+    assert set(syms) == set(_lib.SIGNATURES), set(syms) ^ set(_lib.SIGNATURES)
+
+
+def test_version_and_status_names(nwd):
+    from importlib import import_module
+    _lib = import_module(nwd.__name__ + "._lib")
+    lib = _lib.load()
+    assert "sm_100a" in nwd.version()
+    assert lib.nwd_status_name(0) == b"NWD_OK"
+    assert lib.nwd_status_name(2) == b"NWD_ERR_RANGE"
+    assert lib.nwd_status_name(99) == b"NWD_ERR_UNKNOWN"
+
+
+def test_range_error_before_launch(nwd):
+    """seq >= maxSeq fails like engine/runtime.js:448, with no CUDA call."""
+    from importlib import import_module
+    _lib = import_module(nwd.__name__ + "._lib")
+    lib = _lib.load()
+    dummy = ctypes.c_void_p(16)
+    st = lib.nwd_kv_append(dummy, dummy, 256, 8, 128, 256, None)
+    assert st == _lib.NWD_ERR_RANGE
+    assert lib.nwd_last_error() == b"seq 256 exceeds maxSeq 256"
+    st = lib.nwd_kv_append_attn_decode(dummy, dummy, dummy, dummy, dummy, dummy, 40, 8, 128, 300,
+                                       256, 0.0, dummy, 1 << 20, None)
+    assert st == _lib.NWD_ERR_RANGE
+    assert b"exceeds maxSeq" in lib.nwd_last_error()
+    with pytest.raises(_lib.NwdError, match="seq 256 exceeds maxSeq 256"):
+        _lib.check(lib.nwd_kv_append(dummy, dummy, 256, 8, 128, 256, None))
+
+
+def test_null_pointer_errors(nwd):
+    from importlib import import_module
+    _lib = import_module(nwd.__name__ + "._lib")
+    lib = _lib.load()
+    assert lib.nwd_kv_append(None, None, 0, 8, 128, 256, None) == _lib.NWD_ERR_INVALID
+    assert lib.nwd_attn_merge(None, None, None, 1, 1, 1, 128, None) == _lib.NWD_ERR_INVALID
+    assert lib.nwd_workspace_init(None, 0, None) == _lib.NWD_ERR_WORKSPACE
+    v = ctypes.c_uint32()
+    assert lib.nwd_workspace_check(None, 0, ctypes.byref(v), None) == _lib.NWD_ERR_WORKSPACE
+    assert lib.nwd_attn_decode_workspace_size(1, 40, 8, 128, None) == _lib.NWD_ERR_INVALID
+
+
+def test_shape_errors_before_launch(nwd):
+    from importlib import import_module
+    _lib = import_module(nwd.__name__ + "._lib")
+    lib = _lib.load()
+    sz = ctypes.c_size_t()
+    # group not integral, head_dim unsupported, group too large: all rejected
+    # before the device is queried
+    assert lib.nwd_attn_decode_workspace_size(1, 40, 7, 128, ctypes.byref(sz)) == _lib.NWD_ERR_INVALID
+    assert lib.nwd_attn_decode_workspace_size(1, 40, 8, 64, ctypes.byref(sz)) == _lib.NWD_ERR_UNSUPPORTED
+    assert lib.nwd_attn_decode_workspace_size(1, 32, 2, 128, ctypes.byref(sz)) == _lib.NWD_ERR_UNSUPPORTED
+
+
+def test_ops_reject_cpu_tensors(ops):
+    import torch
+    src = torch.zeros(1024, dtype=torch.float16)
+    cache = torch.zeros(256, 8, 128, dtype=torch.float16)
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        ops.kv_append(src, cache, ops.KvParams(0, 8, 128))
