@@ -15,7 +15,8 @@
 //    O^T += V^T P^T are m16n8k16 tensor-core MMAs with rows (tokens) on M and
 //    query heads on N, fp32 accumulation.  Online softmax in the log2 domain
 //    with shuffle max reductions; P is handed from the score accumulators to
-//    the PV operand with movmatrix (no shared-memory round trip).
+//    the PV operand with movmatrix (no shared-memory round trip), as an fp16
+//    head + fp16 remainder pair (two MMAs) so P keeps ~22 bits.
 //  * End of unit: the four warps merge their (m, l, acc) in shared memory.
 //    A unit that covers its whole sequence writes O (or the shard partial);
 //    otherwise it writes a partial to the workspace and takes a ticket, and
@@ -554,8 +555,16 @@ __global__ void __launch_bounds__(NTHR, 1)
         acc[mt][3] *= al1;
       }
       // ---- P^T fragments for the PV MMA ----
-      const uint32_t pb0 = movmatrix_t(pack_half2(p0, p1));
-      const uint32_t pb1 = movmatrix_t(pack_half2(p2, p3));
+      // P is split into an fp16 head and an fp16 remainder (p = hi + lo to
+      // ~22 bits): a single fp16 rounding of P (2^-11 relative) would exceed
+      // the parity tolerance on outputs near zero.
+      const __half2 h01 = __floats2half2_rn(p0, p1), h23 = __floats2half2_rn(p2, p3);
+      const __half2 r01 = __floats2half2_rn(p0 - __low2float(h01), p1 - __high2float(h01));
+      const __half2 r23 = __floats2half2_rn(p2 - __low2float(h23), p3 - __high2float(h23));
+      const uint32_t pb0 = movmatrix_t(*reinterpret_cast<const uint32_t*>(&h01));
+      const uint32_t pb1 = movmatrix_t(*reinterpret_cast<const uint32_t*>(&h23));
+      const uint32_t pl0 = movmatrix_t(*reinterpret_cast<const uint32_t*>(&r01));
+      const uint32_t pl1 = movmatrix_t(*reinterpret_cast<const uint32_t*>(&r23));
       // rows past `valid` may hold stale or foreign data: zero them in V^T
       uint32_t mlo = 0xffffffffu, mhi = 0xffffffffu;
       if (valid < 16) {
@@ -575,6 +584,7 @@ __global__ void __launch_bounds__(NTHR, 1)
         a2 &= mhi;
         a3 &= mhi;
         mma16816(acc[mt], a0, a1, a2, a3, pb0, pb1);
+        mma16816(acc[mt], a0, a1, a2, a3, pl0, pl1);
       }
     }
     __syncwarp();
@@ -652,21 +662,41 @@ __global__ void __launch_bounds__(NTHR, 1)
         __threadfence();
         const uint32_t u0 = u - (uint32_t)h.c;
         if (g < G) {
+          // one online pass over the chunks in chunk order, 8 chunks' loads in
+          // flight per thread (the merge is L2-latency bound, not bandwidth bound)
           M = -INFINITY;
-          for (uint32_t cc = 0; cc < nch; cc++)
-            M = fmaxf(M, __ldcg(ws_ml + ((size_t)(u0 + cc) * G + g) * 2));
           Ls = 0.f;
 #pragma unroll
           for (int j = 0; j < 8; j++) o8[j] = 0.f;
-          for (uint32_t cc = 0; cc < nch; cc++) {
-            const size_t slot = (size_t)(u0 + cc) * G + g;
-            const float2 ml = __ldcg(reinterpret_cast<const float2*>(ws_ml + slot * 2));
-            const float f = ml.x == -INFINITY ? 0.f : ex2(ml.x - M);
-            Ls += f * ml.y;
-            const float4* src = reinterpret_cast<const float4*>(ws_o + slot * HD + d0);
-            const float4 x0 = __ldcg(src), x1 = __ldcg(src + 1);
-            o8[0] += f * x0.x; o8[1] += f * x0.y; o8[2] += f * x0.z; o8[3] += f * x0.w;
-            o8[4] += f * x1.x; o8[5] += f * x1.y; o8[6] += f * x1.z; o8[7] += f * x1.w;
+          for (uint32_t cc = 0; cc < nch; cc += 8) {
+            float2 ml[8];
+            float4 x0[8], x1[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+              if (cc + j < nch) {
+                const size_t slot = (size_t)(u0 + cc + j) * G + g;
+                ml[j] = __ldcg(reinterpret_cast<const float2*>(ws_ml + slot * 2));
+                const float4* src = reinterpret_cast<const float4*>(ws_o + slot * HD + d0);
+                x0[j] = __ldcg(src);
+                x1[j] = __ldcg(src + 1);
+              } else {
+                ml[j] = make_float2(-INFINITY, 0.f);
+                x0[j] = x1[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+              if (ml[j].x == -INFINITY) continue;  // empty chunk
+              const float Mn = fmaxf(M, ml[j].x);
+              const float a = ex2(M - Mn);  // 0 while M is -inf
+              const float f = ex2(ml[j].x - Mn);
+              Ls = Ls * a + f * ml[j].y;
+              o8[0] = o8[0] * a + f * x0[j].x; o8[1] = o8[1] * a + f * x0[j].y;
+              o8[2] = o8[2] * a + f * x0[j].z; o8[3] = o8[3] * a + f * x0[j].w;
+              o8[4] = o8[4] * a + f * x1[j].x; o8[5] = o8[5] * a + f * x1[j].y;
+              o8[6] = o8[6] * a + f * x1[j].z; o8[7] = o8[7] * a + f * x1[j].w;
+              M = Mn;
+            }
           }
         }
         if (ct == 0) tickets[b * p.n_kv + hkv] = 0u;
@@ -695,11 +725,16 @@ __global__ void __launch_bounds__(NTHR, 1)
 }
 
 // ---------------- host side ----------------
+// Chunk policy: about `waves` units per CTA (one persistent CTA per SM), a
+// chunk at least min_chunk rows and at most max_chunk rows (longer chunks mean
+// fewer partials to merge; the queue balances ragged batches), and never more
+// than cap_per_sm units per SM.  Defaults from a sweep on B200 (config-3
+// ragged batch and config-2 single sequences).
 struct Tuning {
-  uint32_t waves = 4;        // target units per CTA
-  uint32_t cap_per_sm = 64;  // hard cap on units per SM
+  uint32_t waves = 1;
+  uint32_t cap_per_sm = 64;
   uint32_t min_chunk = 256;
-  uint32_t max_chunk = 1024;
+  uint32_t max_chunk = 4096;
 };
 
 uint32_t env_u32(const char* name, uint32_t dflt) {
