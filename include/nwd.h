@@ -110,6 +110,9 @@ int nwd_workspace_check(void* workspace, size_t ws_bytes, uint32_t* device_error
 #define NWD_DEVERR_PIPE_TIMEOUT 1u  /* an mbarrier wait hit its iteration limit */
 #define NWD_DEVERR_ROW_RANGE 2u     /* a row index fell outside the pool */
 
+/* Softmax `scale` below: finite and >= 0; 0 selects the reference's
+ * inverseSqrt(head_dim). */
+
 /* kernels/sparse_attn.wgsl:32-113 — for each query head h:
  *   O[h,:] = softmax(scale * Q[h,:] . K[t, h/group, :]^T, t < seq) . V[t, h/group, :]
  * The first four scalars are the WGSL Params {n_heads, n_kv_heads, head_dim,
@@ -156,11 +159,13 @@ int nwd_kv_append_attn_decode_batched(const uint16_t* q, const uint16_t* k_new,
 
 /* Partial attention over a shard of each sequence's rows, for merging across
  * shards (GPUs).  Same inputs as nwd_attn_decode_batched; instead of O it
- * writes, per (b, h):
- *   part_ml[(b*n_heads+h)*2 + 0] = m = max_t s_t * log2(e)   (log2 units)
- *   part_ml[(b*n_heads+h)*2 + 1] = l = sum_t 2^(s_t*log2(e) - m)
- *   part_o [(b*n_heads+h)*head_dim + i] = sum_t 2^(s_t*log2(e) - m) * V[t,i]
- * with s_t = scale * q.k_t.  An empty shard writes m = -inf, l = 0, o = 0. */
+ * writes, per (b, h), a triple (m, l, o) with
+ *   l * 2^m = sum_t 2^(s_t*log2(e))          o[i] * 2^m = sum_t 2^(s_t*log2(e)) * V[t,i]
+ *   part_ml[(b*n_heads+h)*2 + 0] = m,  part_ml[(b*n_heads+h)*2 + 1] = l,
+ *   part_o [(b*n_heads+h)*head_dim + i] = o[i],
+ * where s_t = scale * q.k_t and m (log2 units) is a reference maximum within
+ * 8 of max_t s_t*log2(e) (m <= the true maximum, so every term is <= 2^8).
+ * An empty shard writes m = -inf, l = 0, o = 0. */
 int nwd_attn_decode_partial(const uint16_t* q, const uint16_t* k_pool, const uint16_t* v_pool,
                             uint64_t pool_rows, const int64_t* row_offset,
                             const int32_t* seq_len, float* part_o, float* part_ml,
@@ -170,7 +175,8 @@ int nwd_attn_decode_partial(const uint16_t* q, const uint16_t* k_pool, const uin
 
 /* Log-sum-exp merge of `shards` partials laid out [shards][batch*n_heads][...]
  * (as nwd_attn_decode_partial writes them) into o [batch, n_heads, head_dim]
- * fp16.  Shards are merged in index order. */
+ * fp16: o = sum_r o_r 2^(m_r - M) / sum_r l_r 2^(m_r - M), M = max_r m_r.
+ * Shards are merged in index order. */
 int nwd_attn_merge(const float* part_o, const float* part_ml, uint16_t* o, uint32_t shards,
                    uint32_t batch, uint32_t n_heads, uint32_t head_dim, void* stream);
 

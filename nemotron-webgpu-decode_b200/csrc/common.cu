@@ -131,9 +131,9 @@ int kv_tensor_map(CUtensorMap* out, const void* base, uint64_t rows, uint32_t n_
 
 static size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-WsLayout ws_layout(uint32_t batch, uint32_t n_kv, uint32_t group, uint32_t hd, uint32_t units_cap) {
+WsLayout ws_layout(uint32_t batch, uint32_t n_kv, uint32_t group, uint32_t hd, uint32_t slots) {
   WsLayout L;
-  L.max_units = units_cap + n_kv * batch;
+  L.max_units = slots;
   L.tickets_off = sizeof(WsHeader);
   size_t off = round_up(L.tickets_off + sizeof(uint32_t) * (size_t)batch * n_kv, 256);
   L.ml_off = off;

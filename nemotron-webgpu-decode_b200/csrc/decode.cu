@@ -3,28 +3,33 @@
 // Restates kernels/sparse_attn.wgsl:32-113 (O = softmax(scale q.K^T) V per
 // query head, kv head = h / group) for B200:
 //
-//  * Work is cut into units (sequence b, kv head, chunk of C rows).  One
-//    persistent CTA per SM pulls units from an atomic queue in the workspace.
-//  * Per CTA: one producer warp streams 64-row K and V tiles of the unit's kv
+//  * Work split (stream-K style): the (sequence, kv head, row) space of the
+//    whole call is flattened, pair by pair, and every persistent CTA (one per
+//    SM) takes one equal contiguous range of it.  A range is cut at pair
+//    boundaries into pieces: pieces covering a whole pair write O directly;
+//    only the pieces at the two ends of a range are partial, so a CTA has at
+//    most two partials to merge and every SM streams the same number of bytes
+//    whatever the length distribution (ragged batches, one long sequence).
+//  * Per CTA: one producer warp streams 64-row K and V tiles of the piece's kv
 //    head into a 5-stage shared-memory ring with TMA (4-D tensor map over the
 //    [rows, n_kv, 128] cache, 128-byte swizzle, no multicast) and mbarrier
-//    transaction counts.  Each unit's first stage also carries the G query
-//    rows of that kv head (1-D bulk copy).
+//    transaction counts.  A piece's first stage also carries the G query rows
+//    of its kv head (1-D bulk copy).
 //  * Four consumer warps each take 16 rows of every stage.  All G <= 8 query
 //    heads of the kv head share each loaded K/V tile: S^T = K Q^T and
 //    O^T += V^T P^T are m16n8k16 tensor-core MMAs with rows (tokens) on M and
 //    query heads on N, fp32 accumulation.  Online softmax in the log2 domain
-//    with shuffle max reductions; P is handed from the score accumulators to
-//    the PV operand with movmatrix (no shared-memory round trip), as an fp16
-//    head + fp16 remainder pair (two MMAs) so P keeps ~22 bits.
-//  * End of unit: the four warps merge their (m, l, acc) in shared memory.
-//    A unit that covers its whole sequence writes O (or the shard partial);
-//    otherwise it writes a partial to the workspace and takes a ticket, and
-//    the CTA holding the last ticket of that (b, kv head) merges all chunks in
-//    chunk order (deterministic) and writes the result.  No CTA ever waits
-//    for another.
-//  * Optional append mode fuses kernels/kv_append.wgsl: the unit that owns
-//    the new row writes it (generic stores + proxy fence) before its TMA
+//    with shuffle max reductions and lazy rescaling; P is handed from the score
+//    accumulators to the PV operand with movmatrix (no shared-memory round
+//    trip), as an fp16 head + fp16 remainder pair (two MMAs) so P keeps ~22
+//    bits.
+//  * End of piece: the four warps merge their (m, l, acc) in shared memory.
+//    A partial piece writes its (m, l, acc) to a workspace slot and takes a
+//    ticket on its pair; the CTA holding the pair's last ticket merges the
+//    pieces in range order (deterministic) and writes the result.  No CTA
+//    ever waits for another.
+//  * Optional append mode fuses kernels/kv_append.wgsl: the piece that ends
+//    at the new row writes it (generic stores + proxy fence) before its TMA
 //    loads read it.
 //
 // Every mbarrier wait is bounded (time and iteration limits); on expiry the
@@ -42,8 +47,10 @@ namespace {
 using nwd::WsHeader;
 
 constexpr int HD = 128;                  // head_dim supported by the tiles
-constexpr int NCW = 4;                   // consumer warps
-constexpr int TOK = 16 * NCW;            // rows per stage
+constexpr int WPG = 4;                   // consumer warps per group (16 rows each)
+constexpr int NGRP = 2;                  // consumer groups, taking alternate stages
+constexpr int NCW = WPG * NGRP;          // consumer warps
+constexpr int TOK = 16 * WPG;            // rows per stage
 constexpr int NST = 5;                   // pipeline stages
 constexpr int GMAX = 8;                  // query heads per kv head (mma N)
 constexpr int NTHR = (NCW + 1) * 32;     // + producer warp
@@ -51,10 +58,13 @@ constexpr int KV_BYTES = TOK * HD * 2;   // one K (or V) stage: 16 KiB
 constexpr int Q_BYTES = GMAX * HD * 2;   // query rows of one kv head
 constexpr int MAXB = 4096;               // sequences per launch
 
-constexpr uint32_t F_FIRST = 1u, F_LAST = 2u;
+// stage header flags
+constexpr int32_t F_FIRST = 1, F_LAST = 2, F_COMPLETE = 4, F_TERM = 8;
 
+// Written by the producer for every stage; `f`..`l` are the CTAs whose ranges
+// cover the stage's (b, hkv) pair, `slot` the workspace slot of a partial piece.
 struct StageHdr {
-  int32_t unit, b, hkv, t0, ntok, flags, nch, c;
+  int32_t b, hkv, t0, ntok, flags, slot, f, l;
 };
 
 struct Params {
@@ -71,13 +81,14 @@ struct Params {
   uint8_t* ws;
   uint64_t pool_rows;
   uint64_t tickets_off, ml_off, o_off;
-  uint32_t max_units;
+  uint32_t nslots;  // partial slots in the workspace (2 per CTA)
   int32_t single_len;
   uint32_t batch, n_heads, n_kv, group;
   float scale_log2;
   uint32_t append;   // seq_len holds the row to write; attend row + 1 rows
   uint32_t partial;  // write (m, l, o) partials instead of O
-  uint32_t units_target, units_cap, min_chunk, max_chunk;
+  uint32_t min_chunk;  // least rows (x kv heads) per CTA range
+  uint32_t pair_max;   // one CTA per (sequence, kv head) when every pair is this short
 };
 
 // ---- shared memory layout (offsets from a 1024-aligned base) ----
@@ -92,17 +103,18 @@ constexpr int OFF_BAR = OFF_HDR + NST * (int)sizeof(StageHdr);
 constexpr int OFF_MISC = OFF_BAR + 2 * NST * 8 + 8;  // + consumer-sync barrier
 constexpr int SMEM_USED = OFF_MISC + 64;
 constexpr int SMEM_BYTES = SMEM_USED + 1024;  // slack for manual 1024-byte alignment
+static_assert(SMEM_BYTES <= 227 * 1024, "exceeds the 227 KiB per-CTA shared memory of sm_100");
 
 struct Misc {
   int32_t abort;
   int32_t last;
-  uint32_t chunk;
-  uint32_t total_units;
   uint32_t warp_sum[NTHR / 32];
+  uint32_t max_rows;
   uint64_t total_rows;
 };
 static_assert(sizeof(Misc) <= 64, "misc block");
 
+constexpr float RESCALE_LOG2 = 8.f;  // lazy-rescale threshold (log2 units)
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s
 constexpr uint32_t WAIT_LIMIT_ITERS = 1u << 26;
 
@@ -234,32 +246,18 @@ __device__ __forceinline__ uint32_t swz(uint32_t R, uint32_t chunk16) {
 }
 
 // ---------------- work plan ----------------
+// Rows attended by sequence b (clamped to the pool so every sum below fits).
 __device__ __forceinline__ uint32_t seq_rows(const Params& p, uint32_t b) {
-  if (!p.seq_len) return p.single_len > 0 ? (uint32_t)p.single_len : 0u;
-  const int32_t v = p.seq_len[b];
-  if (p.append) return v >= 0 ? (uint32_t)v + 1u : 0u;
-  return v > 0 ? (uint32_t)v : 0u;
+  int64_t v;
+  if (!p.seq_len) v = p.single_len;
+  else v = p.append ? (int64_t)p.seq_len[b] + 1 : (int64_t)p.seq_len[b];
+  if (v <= 0) return 0u;
+  return (uint64_t)v > p.pool_rows ? (uint32_t)p.pool_rows : (uint32_t)v;
 }
 __device__ __forceinline__ int64_t seq_off(const Params& p, uint32_t b) {
   return p.row_offset ? p.row_offset[b] : 0;
 }
 __device__ __forceinline__ uint32_t cdiv(uint64_t a, uint64_t b) { return (uint32_t)((a + b - 1) / b); }
-
-// Chunk length C (multiple of TOK): about units_target units overall, at
-// least min_chunk rows, at most max_chunk rows unless that would exceed
-// units_cap units.  Identical in every CTA.
-__device__ uint32_t choose_chunk(const Params& p, uint64_t total_rows) {
-  const uint64_t work = total_rows * p.n_kv;
-  uint64_t c = (work + p.units_target - 1) / p.units_target;
-  c = (c + TOK - 1) / TOK * TOK;
-  if (c < p.min_chunk) c = p.min_chunk;
-  if (c > p.max_chunk) c = p.max_chunk;
-  uint64_t cu = (work + p.units_cap - 1) / p.units_cap;
-  cu = (cu + TOK - 1) / TOK * TOK;
-  if (c < cu) c = cu;
-  if (c > 0x40000000ull) c = 0x40000000ull;
-  return (uint32_t)c;
-}
 
 // Block-wide exclusive scan of per-thread values; returns this thread's
 // offset, writes the grand total to *total (all threads see it after return).
@@ -285,24 +283,31 @@ __device__ uint32_t block_scan(uint32_t v, Misc* misc, uint32_t* total) {
   return before + x - v;
 }
 
-__device__ __forceinline__ uint32_t find_seq(const uint32_t* pfx, uint32_t batch, uint32_t u) {
-  // largest b with pfx[b] <= u
-  uint32_t lo = 0, hi = batch;  // pfx[batch] = total > u
+// Largest b < batch with S[b] <= y (S non-decreasing, S[batch] > y): the
+// sequence whose rows contain flattened row y.  Empty sequences never match.
+__device__ __forceinline__ uint32_t find_seq(const uint32_t* S, uint32_t batch, uint64_t y) {
+  uint32_t lo = 0, hi = batch;
   while (hi - lo > 1) {
     const uint32_t mid = (lo + hi) >> 1;
-    if (pfx[mid] <= u) lo = mid; else hi = mid;
+    if ((uint64_t)S[mid] <= y) lo = mid; else hi = mid;
   }
   return lo;
 }
 
 // ---------------- kernel ----------------
+// 64-bit quotient with a 32-bit fast path (most operands fit).
+__device__ __forceinline__ uint64_t udiv64(uint64_t a, uint64_t b) {
+  if ((a >> 32) == 0 && (b >> 32) == 0) return (uint32_t)a / (uint32_t)b;
+  return a / b;
+}
+
 __global__ void __launch_bounds__(NTHR, 1)
     decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                   const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sbase = smem_u32(smem);
-  uint32_t* pfx = reinterpret_cast<uint32_t*>(smem + OFF_PFX);
+  uint32_t* S = reinterpret_cast<uint32_t*>(smem + OFF_PFX);  // row prefix over sequences
   StageHdr* hdr = reinterpret_cast<StageHdr*>(smem + OFF_HDR);
   Misc* misc = reinterpret_cast<Misc*>(smem + OFF_MISC);
   volatile int32_t* abort_flag = &misc->abort;
@@ -318,15 +323,16 @@ __global__ void __launch_bounds__(NTHR, 1)
   const uint32_t B = p.seq_len ? p.batch : 1u;
   const uint32_t G = p.group;
 
-  // ---- plan: total rows -> chunk -> per-sequence unit prefix ----
+  // ---- plan: row prefix S over sequences (S[b] = rows before b) ----
   if (tid == 0) {
     misc->abort = 0;
     misc->last = 0;
     misc->total_rows = 0;
+    misc->max_rows = 0;
 #pragma unroll
     for (int s = 0; s < NST; s++) {
       mbar_init(bar_full + 8 * s, 1);
-      mbar_init(bar_empty + 8 * s, NCW);
+      mbar_init(bar_empty + 8 * s, WPG);
     }
     mbar_init(bar_csync, NCW * 32);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -335,95 +341,121 @@ __global__ void __launch_bounds__(NTHR, 1)
   const uint32_t seg = (B + NTHR - 1) / NTHR;
   const uint32_t beg = min(B, tid * seg), end = min(B, beg + seg);
   uint64_t rows_local = 0;
-  for (uint32_t b = beg; b < end; b++) rows_local += seq_rows(p, b);
+  uint32_t max_local = 0;
+  for (uint32_t b = beg; b < end; b++) {
+    const uint32_t L = seq_rows(p, b);
+    rows_local += L;
+    max_local = max(max_local, L);
+  }
   if (rows_local)
     atomicAdd(reinterpret_cast<unsigned long long*>(&misc->total_rows),
               (unsigned long long)rows_local);
-  __syncthreads();
-  const uint64_t total_rows = misc->total_rows;
-  const uint32_t C = choose_chunk(p, total_rows);
-  uint32_t units_local = 0;
-  for (uint32_t b = beg; b < end; b++) {
-    const uint32_t L = seq_rows(p, b);
-    units_local += p.n_kv * max(1u, cdiv(L, C));
-  }
-  uint32_t total_units;
-  uint32_t run = block_scan(units_local, misc, &total_units);
-  for (uint32_t b = beg; b < end; b++) {
-    pfx[b] = run;
-    run += p.n_kv * max(1u, cdiv(seq_rows(p, b), C));
-  }
-  if (tid == 0) pfx[B] = total_units;
-  if (total_units > p.max_units) {
+  if (max_local) atomicMax(&misc->max_rows, max_local);
+  uint32_t total32;
+  uint32_t run = block_scan((uint32_t)rows_local, misc, &total32);  // syncs: sums final
+  if (misc->total_rows >= (1ull << 32)) {
+    // more than 2^32 rows in one call: refuse (uniform across the block)
     if (tid == 0 && blockIdx.x == 0) atomicOr(&wsh->error, NWD_DEVERR_ROW_RANGE);
-    return;  // uniform across the block; nothing launched yet
+    return;
   }
+  for (uint32_t b = beg; b < end; b++) {
+    S[b] = run;
+    run += seq_rows(p, b);
+  }
+  if (tid == 0) S[B] = total32;
   __syncthreads();
+  // Work split.  Pair mode (small problems): CTA i takes the whole pair i, no
+  // partials.  Otherwise every CTA takes an equal range [x0, x1) of the
+  // flattened (pair, row) space, T = n_kv * all rows.
+  const bool pair_mode = (uint64_t)B * p.n_kv <= gridDim.x && misc->max_rows <= p.pair_max;
+  const uint64_t T = (uint64_t)p.n_kv * total32;
+  uint64_t W = udiv64(T + gridDim.x - 1, gridDim.x);
+  if (W < p.min_chunk) W = p.min_chunk;
+  const uint64_t x0 = min(T, (uint64_t)blockIdx.x * W);
+  const uint64_t x1 = min(T, x0 + W);
+
+  // Empty sequences produce no rows, so no range covers them: CTA b % grid
+  // writes their result (zeros, as the WGSL's untouched accumulator; or an
+  // empty partial m = -inf, l = 0, o = 0).
+  for (uint32_t b = blockIdx.x; b < B; b += gridDim.x) {
+    if (S[b + 1] != S[b]) continue;
+    if (p.append && tid == 0) atomicOr(&wsh->error, NWD_DEVERR_ROW_RANGE);  // pos < 0
+    const size_t row0 = (size_t)b * p.n_heads;
+    for (uint32_t i = tid; i < p.n_heads * (HD / 8); i += NTHR) {
+      const size_t row = row0 + i / (HD / 8), d = (i % (HD / 8)) * 8;
+      if (p.partial) {
+        float4* dst = reinterpret_cast<float4*>(p.part_o + row * HD + d);
+        dst[0] = dst[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (d == 0) *reinterpret_cast<float2*>(p.part_ml + row * 2) = make_float2(-INFINITY, 0.f);
+      } else {
+        *reinterpret_cast<uint4*>(p.o + row * HD + d) = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+  }
 
   if (warp == NCW) {
     // ======================= producer warp =======================
+    // Stages are numbered c = 0, 1, 2, ... (ring slot c % NST); consumer group
+    // c & 1 takes stage c.  Every piece gets an even number of stages (an
+    // empty one pads odd counts), so both groups see a first and a last stage
+    // of every piece.
     const uint64_t policy = evict_first_policy();
-    int stage = 0;
+    int slot = 0;
     uint32_t phase = 0;
-    uint32_t n_issued = 0;  // stages armed so far (stage s armed ceil((n-s)/NST) times)
+    uint32_t n_issued = 0;  // stages armed so far (slot s armed ceil((n-s)/NST) times)
     bool aborted = false;
-    while (!aborted) {
-      uint32_t u = 0;
-      if (lane == 0) u = atomicAdd(&wsh->next_unit, 1u);
-      u = __shfl_sync(0xffffffffu, u, 0);
-      if (u >= total_units) break;
-      const uint32_t b = find_seq(pfx, B, u);
-      const uint32_t L = seq_rows(p, b);
-      const uint32_t nch = (pfx[b + 1] - pfx[b]) / p.n_kv;
-      const uint32_t r = u - pfx[b];
-      const uint32_t hkv = r / nch, c = r % nch;
+
+    // emits one piece: rows [t0, t1) of pair (b, hkv)
+    auto emit_piece = [&](uint32_t b, uint32_t hkv, uint32_t L, uint32_t t0, uint32_t t1,
+                          bool complete, int32_t f, int32_t l) {
+      const int32_t pslot = (int32_t)(2u * blockIdx.x + (t0 > 0 ? 0u : 1u));
       const int64_t off = seq_off(p, b);
-      const uint32_t t_begin = c * C;
-      const uint32_t t_end = min(L, t_begin + C);
-      if (lane == 0 && c == 0 && (off < 0 || (uint64_t)off + L > p.pool_rows))
+      if (lane == 0 && t0 == 0 && hkv == 0 && (off < 0 || (uint64_t)off + L > p.pool_rows))
         atomicOr(&wsh->error, NWD_DEVERR_ROW_RANGE);
-      if (p.append && c == nch - 1 && L > 0) {
-        // fused kv_append: this unit owns row L-1 of kv head hkv
+      if (p.append && t1 == L) {
+        // fused kv_append: this piece ends at the new row L-1 of kv head hkv
         const int64_t row = off + (int64_t)L - 1;
         if (row >= 0 && (uint64_t)row < p.pool_rows) {
           const size_t dst = ((size_t)row * p.n_kv + hkv) * HD;
           const size_t src = ((size_t)b * p.n_kv + hkv) * HD;
           const int half = lane >> 4, j = lane & 15;  // lanes 0-15: K, 16-31: V
-          const uint4* s = reinterpret_cast<const uint4*>((half ? p.v_new : p.k_new) + src) + j;
-          uint4* d = reinterpret_cast<uint4*>((half ? p.v_pool : p.k_pool) + dst) + j;
-          *d = __ldg(s);
+          const uint4* sp = reinterpret_cast<const uint4*>((half ? p.v_new : p.k_new) + src) + j;
+          uint4* dp = reinterpret_cast<uint4*>((half ? p.v_pool : p.k_pool) + dst) + j;
+          *dp = __ldg(sp);
           asm volatile("fence.proxy.async;" ::: "memory");
         } else if (lane == 0) {
           atomicOr(&wsh->error, NWD_DEVERR_ROW_RANGE);
         }
         __syncwarp();
       }
-      const uint32_t nstages = t_end > t_begin ? cdiv(t_end - t_begin, TOK) : 1u;
-      for (uint32_t s = 0; s < nstages; s++) {
-        if (!warp_wait(bar_empty + 8 * stage, phase ^ 1u, abort_flag, &wsh->error)) {
+      const uint32_t nreal = cdiv(t1 - t0, TOK);
+      const uint32_t nstages = (nreal + 1u) & ~1u;
+      for (uint32_t s = 0; s < nstages && !aborted; s++) {
+        if (!warp_wait(bar_empty + 8 * slot, phase ^ 1u, abort_flag, &wsh->error)) {
           aborted = true;
           break;
         }
         if (lane == 0) {
           StageHdr h;
-          h.unit = (int32_t)u;
           h.b = (int32_t)b;
           h.hkv = (int32_t)hkv;
-          h.t0 = (int32_t)(t_begin + s * TOK);
-          h.ntok = (int32_t)(t_end > t_begin ? min((uint32_t)TOK, t_end - (t_begin + s * TOK)) : 0u);
-          h.flags = (s == 0 ? F_FIRST : 0u) | (s + 1 == nstages ? F_LAST : 0u);
-          h.nch = (int32_t)nch;
-          h.c = (int32_t)c;
-          hdr[stage] = h;
-          const uint32_t fb = bar_full + 8 * stage;
+          h.t0 = (int32_t)(t0 + s * TOK);
+          h.ntok = s < nreal ? (int32_t)min((uint32_t)TOK, t1 - (t0 + s * TOK)) : 0;
+          h.flags = (s < 2 ? F_FIRST : 0) | (s + 2 >= nstages ? F_LAST : 0) |
+                    (complete ? F_COMPLETE : 0);
+          h.slot = pslot;
+          h.f = f;
+          h.l = l;
+          hdr[slot] = h;
+          const uint32_t fb = bar_full + 8 * slot;
           if (h.ntok > 0) {
-            const uint32_t qbytes = (s == 0) ? G * HD * 2 : 0u;
+            const uint32_t qbytes = (s < 2) ? G * HD * 2 : 0u;
             mbar_arrive_tx(fb, 2 * KV_BYTES + qbytes);
             const int row = (int)(off + (int64_t)h.t0);
-            tma_load_4d(sbase + OFF_K + stage * KV_BYTES, &tmk, fb, 0, 0, (int)hkv, row, policy);
-            tma_load_4d(sbase + OFF_V + stage * KV_BYTES, &tmv, fb, 0, 0, (int)hkv, row, policy);
+            tma_load_4d(sbase + OFF_K + slot * KV_BYTES, &tmk, fb, 0, 0, (int)hkv, row, policy);
+            tma_load_4d(sbase + OFF_V + slot * KV_BYTES, &tmv, fb, 0, 0, (int)hkv, row, policy);
             if (qbytes)
-              bulk_load(sbase + OFF_Q + stage * Q_BYTES,
+              bulk_load(sbase + OFF_Q + slot * Q_BYTES,
                         p.q + ((size_t)b * p.n_heads + (size_t)hkv * G) * HD, qbytes, fb);
           } else {
             mbar_arrive(fb);
@@ -431,22 +463,68 @@ __global__ void __launch_bounds__(NTHR, 1)
         }
         __syncwarp();
         n_issued++;
-        if (++stage == NST) {
-          stage = 0;
+        if (++slot == NST) {
+          slot = 0;
           phase ^= 1u;
+        }
+      }
+    };
+
+    if (pair_mode) {
+      const uint32_t i = blockIdx.x;
+      if (i < B * p.n_kv) {
+        const uint32_t b = i / p.n_kv, hkv = i % p.n_kv;
+        const uint32_t L = S[b + 1] - S[b];
+        if (L > 0) emit_piece(b, hkv, L, 0, L, true, (int32_t)i, (int32_t)i);
+      }
+    } else if (x0 < x1) {
+      // locate the first piece, then walk pairs forward (no further division
+      // except for the last pair's CTA span)
+      uint32_t b = find_seq(S, B, udiv64(x0, p.n_kv));
+      uint32_t L = S[b + 1] - S[b];
+      const uint64_t r = x0 - (uint64_t)p.n_kv * S[b];
+      uint32_t hkv = (uint32_t)udiv64(r, L);
+      uint32_t t0 = (uint32_t)(r - (uint64_t)hkv * L);
+      uint64_t pstart = x0 - t0;
+      int32_t f = (int32_t)udiv64(pstart, W);
+      for (uint64_t x = x0; x < x1 && !aborted;) {
+        const uint64_t len = min((uint64_t)(L - t0), x1 - x);
+        const uint32_t t1 = t0 + (uint32_t)len;
+        const bool complete = (t0 == 0 && t1 == L);
+        const int32_t l = (t1 == L) ? (int32_t)blockIdx.x : (int32_t)udiv64(pstart + L - 1, W);
+        emit_piece(b, hkv, L, t0, t1, complete, f, l);
+        x += len;
+        if (x >= x1) break;
+        // next pair starts inside this range
+        pstart = x;
+        t0 = 0;
+        f = (int32_t)blockIdx.x;
+        if (++hkv == p.n_kv) {
+          hkv = 0;
+          do {
+            b++;
+          } while (b + 1 < B && S[b + 1] == S[b]);
+          L = S[b + 1] - S[b];
         }
       }
     }
     if (!aborted) {
-      // terminator stage
-      if (warp_wait(bar_empty + 8 * stage, phase ^ 1u, abort_flag, &wsh->error)) {
-        if (lane == 0) {
-          hdr[stage].unit = -1;
-          mbar_arrive(bar_full + 8 * stage);
+      // one terminator stage per consumer group (the stage count is even here)
+      for (int k = 0; k < NGRP && !aborted; k++) {
+        if (warp_wait(bar_empty + 8 * slot, phase ^ 1u, abort_flag, &wsh->error)) {
+          if (lane == 0) {
+            hdr[slot].flags = F_TERM;
+            mbar_arrive(bar_full + 8 * slot);
+          }
+          __syncwarp();
+          n_issued++;
+          if (++slot == NST) {
+            slot = 0;
+            phase ^= 1u;
+          }
+        } else {
+          aborted = true;
         }
-        __syncwarp();
-      } else {
-        aborted = true;
       }
     }
     if (aborted) {
@@ -460,40 +538,37 @@ __global__ void __launch_bounds__(NTHR, 1)
           }
         }
     }
-    if (lane == 0) {
-      __threadfence();
-      if (atomicAdd(&wsh->done_ctas, 1u) == gridDim.x - 1) {
-        // every CTA has drawn its last unit: reset the queue for the next call
-        wsh->next_unit = 0;
-        wsh->done_ctas = 0;
-        __threadfence();
-      }
-    }
     return;
   }
 
   // ======================= consumer warps =======================
+  const uint32_t grp = warp / WPG, wig = warp % WPG;  // group; 16-row slice of a stage
   const uint32_t g0 = 2u * (lane & 3);      // this lane's two heads (C/B fragment cols)
   const uint32_t rowq = lane >> 2;          // fragment row
   // ldmatrix lane roles
   const uint32_t li = lane >> 3, lr = lane & 7;
-  const uint32_t tokK = warp * 16 + (li & 1) * 8 + lr;  // K: matrices (rows 0-7/8-15) x (k lo/hi)
-  const uint32_t tokV = warp * 16 + (li >> 1) * 8 + lr; // V^T: (d lo/hi) x (tokens lo/hi)
+  const uint32_t tokK = wig * 16 + (li & 1) * 8 + lr;  // K: matrices (rows 0-7/8-15) x (k lo/hi)
+  const uint32_t tokV = wig * 16 + (li >> 1) * 8 + lr; // V^T: (d lo/hi) x (tokens lo/hi)
 
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   float acc[8][4];
   uint32_t qf[8][2];
-  int stage = 0;
-  uint32_t phase = 0, cph = 0;
+  // this group's stages: c = grp, grp + 2, ... -> ring slot and phase
+  uint32_t slot = grp, phase = 0, cph = 0;
   float* mrg = reinterpret_cast<float*>(smem + OFF_MRG);
   float* mrg_m = mrg;                       // [NCW][GMAX]
   float* mrg_l = mrg + NCW * GMAX;          // [NCW][GMAX]
   float* mrg_acc = mrg + 2 * NCW * GMAX;    // [NCW][GMAX][HD]
 
   while (true) {
-    if (!warp_wait(bar_full + 8 * stage, phase, abort_flag, &wsh->error)) break;
-    const StageHdr h = hdr[stage];
-    if (h.unit < 0) break;
+    // Consecutive uses of a ring slot alternate between the two groups (NST
+    // is odd).  A parity wait cannot tell phase k from phase k+2, so first
+    // wait until the slot's previous use (the other group's stage) has been
+    // released: then the full barrier is at most one phase behind this wait.
+    if (!warp_wait(bar_empty + 8 * slot, phase ^ 1u, abort_flag, &wsh->error)) break;
+    if (!warp_wait(bar_full + 8 * slot, phase, abort_flag, &wsh->error)) break;
+    const StageHdr h = hdr[slot];
+    if (h.flags & F_TERM) break;
     if (h.flags & F_FIRST) {
       m0 = m1 = -INFINITY;
       l0 = l1 = 0.f;
@@ -502,7 +577,7 @@ __global__ void __launch_bounds__(NTHR, 1)
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[mt][j] = 0.f;
       if (h.ntok > 0) {
-        const uint8_t* qs = smem + OFF_Q + stage * Q_BYTES + rowq * (HD * 2) + g0 * 2;
+        const uint8_t* qs = smem + OFF_Q + slot * Q_BYTES + rowq * (HD * 2) + g0 * 2;
         const bool live = rowq < G;
 #pragma unroll
         for (int ks = 0; ks < 8; ks++) {
@@ -511,49 +586,75 @@ __global__ void __launch_bounds__(NTHR, 1)
         }
       }
     }
-    const int valid = min(16, h.ntok - warp * 16);
+    const int valid = min(16, h.ntok - (int)wig * 16);
     if (valid > 0) {
-      const uint32_t kb = sbase + OFF_K + stage * KV_BYTES;
-      const uint32_t vb = sbase + OFF_V + stage * KV_BYTES;
-      // ---- S^T[16 tokens][8 heads] = K Q^T ----
-      float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint32_t kb = sbase + OFF_K + slot * KV_BYTES;
+      const uint32_t vb = sbase + OFF_V + slot * KV_BYTES;
+      // Issue every shared-memory fragment load of the tile up front (K for
+      // S^T = K Q^T, V^T for O^T += V^T P^T) so their latency overlaps the
+      // QK MMAs and the softmax instead of sitting on the critical path.
+      uint32_t ka[8][4], va[8][4];
 #pragma unroll
       for (int ks = 0; ks < 8; ks++) {
         const uint32_t R = 2u * tokK + (uint32_t)(ks >> 2);
         const uint32_t ch = (uint32_t)(ks & 3) * 2u + (li >> 1);
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4(kb + swz(R, ch), a0, a1, a2, a3);
-        mma16816((ks & 1) ? s1 : s0, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+        ldsm_x4(kb + swz(R, ch), ka[ks][0], ka[ks][1], ka[ks][2], ka[ks][3]);
       }
-      float sc[4];
 #pragma unroll
-      for (int j = 0; j < 4; j++) sc[j] = (s0[j] + s1[j]) * p.scale_log2;
-      if ((int)rowq >= valid) sc[0] = sc[1] = -INFINITY;
-      if ((int)rowq + 8 >= valid) sc[2] = sc[3] = -INFINITY;
-      // ---- online softmax (log2 domain), per head column ----
-      float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
+      for (int mt = 0; mt < 8; mt++) {
+        const uint32_t R = 2u * tokV + (uint32_t)(mt >> 2);
+        const uint32_t ch = (uint32_t)(mt & 3) * 2u + (li & 1);
+        ldsm_x4_t(vb + swz(R, ch), va[mt][0], va[mt][1], va[mt][2], va[mt][3]);
+      }
+      // ---- S^T[16 tokens][8 heads] = K Q^T (two accumulator chains) ----
+      float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int ks = 0; ks < 8; ks++)
+        mma16816((ks & 1) ? s1 : s0, ka[ks][0], ka[ks][1], ka[ks][2], ka[ks][3], qf[ks][0],
+                 qf[ks][1]);
+      float sr[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) sr[j] = s0[j] + s1[j];
+      if ((int)rowq >= valid) sr[0] = sr[1] = -INFINITY;
+      if ((int)rowq + 8 >= valid) sr[2] = sr[3] = -INFINITY;
+      // ---- online softmax in the log2 domain, per head column ----
+      // tile max of the raw scores; the scale is positive, so it commutes
+      float mx0 = fmaxf(sr[0], sr[2]), mx1 = fmaxf(sr[1], sr[3]);
 #pragma unroll
       for (int o = 4; o < 32; o <<= 1) {
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
       }
-      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-      const float base0 = mn0 == -INFINITY ? 0.f : mn0;
-      const float base1 = mn1 == -INFINITY ? 0.f : mn1;
-      const float al0 = ex2(m0 - base0), al1 = ex2(m1 - base1);
-      const float p0 = ex2(sc[0] - base0), p1 = ex2(sc[1] - base1);
-      const float p2 = ex2(sc[2] - base0), p3 = ex2(sc[3] - base1);
-      l0 = l0 * al0 + (p0 + p2);
-      l1 = l1 * al1 + (p1 + p3);
-      m0 = mn0;
-      m1 = mn1;
+      mx0 *= p.scale_log2;
+      mx1 *= p.scale_log2;
+      // Lazy rescale: the reference max m only moves when a head's tile max
+      // exceeds it by more than 2^RESCALE_LOG2, so P stays <= 2^8 and the
+      // accumulators are rescaled rarely (the result o / l does not depend
+      // on which m is used).
+      const bool up0 = mx0 > m0 + RESCALE_LOG2, up1 = mx1 > m1 + RESCALE_LOG2;
+      if (__any_sync(0xffffffffu, up0 || up1)) {
+        const float al0 = up0 ? ex2(m0 - mx0) : 1.f;  // 0 while m is -inf
+        const float al1 = up1 ? ex2(m1 - mx1) : 1.f;
+        if (up0) m0 = mx0;
+        if (up1) m1 = mx1;
+        l0 *= al0;
+        l1 *= al1;
 #pragma unroll
-      for (int mt = 0; mt < 8; mt++) {
-        acc[mt][0] *= al0;
-        acc[mt][1] *= al1;
-        acc[mt][2] *= al0;
-        acc[mt][3] *= al1;
+        for (int mt = 0; mt < 8; mt++) {
+          acc[mt][0] *= al0;
+          acc[mt][1] *= al1;
+          acc[mt][2] *= al0;
+          acc[mt][3] *= al1;
+        }
       }
+      const float nb0 = m0 == -INFINITY ? 0.f : -m0;
+      const float nb1 = m1 == -INFINITY ? 0.f : -m1;
+      const float p0 = ex2(fmaf(sr[0], p.scale_log2, nb0));
+      const float p1 = ex2(fmaf(sr[1], p.scale_log2, nb1));
+      const float p2 = ex2(fmaf(sr[2], p.scale_log2, nb0));
+      const float p3 = ex2(fmaf(sr[3], p.scale_log2, nb1));
+      l0 += p0 + p2;
+      l1 += p1 + p3;
       // ---- P^T fragments for the PV MMA ----
       // P is split into an fp16 head and an fp16 remainder (p = hi + lo to
       // ~22 bits): a single fp16 rounding of P (2^-11 relative) would exceed
@@ -565,37 +666,38 @@ __global__ void __launch_bounds__(NTHR, 1)
       const uint32_t pb1 = movmatrix_t(*reinterpret_cast<const uint32_t*>(&h23));
       const uint32_t pl0 = movmatrix_t(*reinterpret_cast<const uint32_t*>(&r01));
       const uint32_t pl1 = movmatrix_t(*reinterpret_cast<const uint32_t*>(&r23));
-      // rows past `valid` may hold stale or foreign data: zero them in V^T
-      uint32_t mlo = 0xffffffffu, mhi = 0xffffffffu;
       if (valid < 16) {
+        // rows past `valid` may hold stale or foreign data: zero them in V^T
         const int te = (int)g0;  // tokens te, te+1 (regs 0,1) and te+8, te+9 (regs 2,3)
-        mlo = (te < valid ? 0x0000ffffu : 0u) | (te + 1 < valid ? 0xffff0000u : 0u);
-        mhi = (te + 8 < valid ? 0x0000ffffu : 0u) | (te + 9 < valid ? 0xffff0000u : 0u);
+        const uint32_t mlo = (te < valid ? 0x0000ffffu : 0u) | (te + 1 < valid ? 0xffff0000u : 0u);
+        const uint32_t mhi =
+            (te + 8 < valid ? 0x0000ffffu : 0u) | (te + 9 < valid ? 0xffff0000u : 0u);
+#pragma unroll
+        for (int mt = 0; mt < 8; mt++) {
+          va[mt][0] &= mlo;
+          va[mt][1] &= mlo;
+          va[mt][2] &= mhi;
+          va[mt][3] &= mhi;
+        }
       }
       // ---- O^T[128 dims][8 heads] += V^T P^T ----
 #pragma unroll
-      for (int mt = 0; mt < 8; mt++) {
-        const uint32_t R = 2u * tokV + (uint32_t)(mt >> 2);
-        const uint32_t ch = (uint32_t)(mt & 3) * 2u + (li & 1);
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4_t(vb + swz(R, ch), a0, a1, a2, a3);
-        a0 &= mlo;
-        a1 &= mlo;
-        a2 &= mhi;
-        a3 &= mhi;
-        mma16816(acc[mt], a0, a1, a2, a3, pb0, pb1);
-        mma16816(acc[mt], a0, a1, a2, a3, pl0, pl1);
-      }
+      for (int mt = 0; mt < 8; mt++)
+        mma16816(acc[mt], va[mt][0], va[mt][1], va[mt][2], va[mt][3], pb0, pb1);
+#pragma unroll
+      for (int mt = 0; mt < 8; mt++)
+        mma16816(acc[mt], va[mt][0], va[mt][1], va[mt][2], va[mt][3], pl0, pl1);
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(bar_empty + 8 * stage);
-    if (++stage == NST) {
-      stage = 0;
+    if (lane == 0) mbar_arrive(bar_empty + 8 * slot);
+    slot += NGRP;
+    if (slot >= NST) {
+      slot -= NST;
       phase ^= 1u;
     }
     if (!(h.flags & F_LAST)) continue;
 
-    // ======== end of unit: merge the four warps, then emit ========
+    // ======== end of piece: merge the eight warps, then emit ========
     float lt0 = l0, lt1 = l1;
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
@@ -620,121 +722,115 @@ __global__ void __launch_bounds__(NTHR, 1)
       }
     }
     if (!consumer_sync(bar_csync, cph, abort_flag, &wsh->error)) break;
+    // 256 threads: head g, dims d0 .. d0+3
     const uint32_t ct = warp * 32 + lane;
-    const uint32_t g = ct >> 4, d0 = (ct & 15) * 8;
+    const uint32_t g = ct >> 5, d0 = (ct & 31) * 4;
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < NCW; w++) M = fmaxf(M, mrg_m[w * GMAX + g]);
-    float Ls = 0.f, o8[8];
-#pragma unroll
-    for (int j = 0; j < 8; j++) o8[j] = 0.f;
+    float Ls = 0.f, o4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int w = 0; w < NCW; w++) {
       const float mw = mrg_m[w * GMAX + g];
       const float f = mw == -INFINITY ? 0.f : ex2(mw - M);
       Ls += f * mrg_l[w * GMAX + g];
-      const float* a = mrg_acc + ((size_t)w * GMAX + g) * HD + d0;
-#pragma unroll
-      for (int j = 0; j < 8; j++) o8[j] += f * a[j];
+      const float4 a = *reinterpret_cast<const float4*>(mrg_acc + ((size_t)w * GMAX + g) * HD + d0);
+      o4[0] += f * a.x;
+      o4[1] += f * a.y;
+      o4[2] += f * a.z;
+      o4[3] += f * a.w;
     }
     if (!consumer_sync(bar_csync, cph, abort_flag, &wsh->error)) break;  // scratch free again
 
-    const uint32_t b = (uint32_t)h.b, hkv = (uint32_t)h.hkv, nch = (uint32_t)h.nch;
-    bool emit = (nch == 1);
+    const uint32_t b = (uint32_t)h.b, hkv = (uint32_t)h.hkv;
+    bool emit = (h.flags & F_COMPLETE) != 0;
     if (!emit) {
-      const uint32_t u = (uint32_t)h.unit;
+      // partial piece: publish it, take a ticket on the pair; the last of the
+      // pair's l - f + 1 pieces merges them in range order
       if (g < G) {
-        const size_t slot = (size_t)u * G + g;
-        *reinterpret_cast<float2*>(ws_ml + slot * 2) = make_float2(M, Ls);
-        float4* dst = reinterpret_cast<float4*>(ws_o + slot * HD + d0);
-        dst[0] = make_float4(o8[0], o8[1], o8[2], o8[3]);
-        dst[1] = make_float4(o8[4], o8[5], o8[6], o8[7]);
+        const size_t sl = (size_t)h.slot * G + g;
+        if (d0 == 0) *reinterpret_cast<float2*>(ws_ml + sl * 2) = make_float2(M, Ls);
+        *reinterpret_cast<float4*>(ws_o + sl * HD + d0) = make_float4(o4[0], o4[1], o4[2], o4[3]);
       }
       __threadfence();
       if (!consumer_sync(bar_csync, cph, abort_flag, &wsh->error)) break;
       if (ct == 0) {
         const uint32_t t = atomicAdd(&tickets[b * p.n_kv + hkv], 1u);
-        misc->last = (t == nch - 1) ? 1 : 0;
+        misc->last = (t == (uint32_t)(h.l - h.f)) ? 1 : 0;
       }
       if (!consumer_sync(bar_csync, cph, abort_flag, &wsh->error)) break;
       emit = misc->last != 0;
       if (emit) {
         __threadfence();
-        const uint32_t u0 = u - (uint32_t)h.c;
         if (g < G) {
-          // one online pass over the chunks in chunk order, 8 chunks' loads in
-          // flight per thread (the merge is L2-latency bound, not bandwidth bound)
+          // one online pass over the pieces, 8 pieces' loads in flight per
+          // thread (the merge is L2-latency bound, not bandwidth bound)
           M = -INFINITY;
           Ls = 0.f;
 #pragma unroll
-          for (int j = 0; j < 8; j++) o8[j] = 0.f;
-          for (uint32_t cc = 0; cc < nch; cc += 8) {
+          for (int j = 0; j < 4; j++) o4[j] = 0.f;
+          for (int32_t c0 = h.f; c0 <= h.l; c0 += 8) {
             float2 ml[8];
-            float4 x0[8], x1[8];
+            float4 x[8];
 #pragma unroll
             for (int j = 0; j < 8; j++) {
-              if (cc + j < nch) {
-                const size_t slot = (size_t)(u0 + cc + j) * G + g;
-                ml[j] = __ldcg(reinterpret_cast<const float2*>(ws_ml + slot * 2));
-                const float4* src = reinterpret_cast<const float4*>(ws_o + slot * HD + d0);
-                x0[j] = __ldcg(src);
-                x1[j] = __ldcg(src + 1);
+              const int32_t c = c0 + j;
+              if (c <= h.l) {
+                // CTA f holds the pair's head in its tail slot; later CTAs in their head slot
+                const size_t sl = (size_t)(2 * c + (c == h.f ? 1 : 0)) * G + g;
+                ml[j] = __ldcg(reinterpret_cast<const float2*>(ws_ml + sl * 2));
+                x[j] = __ldcg(reinterpret_cast<const float4*>(ws_o + sl * HD + d0));
               } else {
                 ml[j] = make_float2(-INFINITY, 0.f);
-                x0[j] = x1[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                x[j] = make_float4(0.f, 0.f, 0.f, 0.f);
               }
             }
 #pragma unroll
             for (int j = 0; j < 8; j++) {
-              if (ml[j].x == -INFINITY) continue;  // empty chunk
+              if (ml[j].x == -INFINITY) continue;  // empty piece
               const float Mn = fmaxf(M, ml[j].x);
               const float a = ex2(M - Mn);  // 0 while M is -inf
               const float f = ex2(ml[j].x - Mn);
               Ls = Ls * a + f * ml[j].y;
-              o8[0] = o8[0] * a + f * x0[j].x; o8[1] = o8[1] * a + f * x0[j].y;
-              o8[2] = o8[2] * a + f * x0[j].z; o8[3] = o8[3] * a + f * x0[j].w;
-              o8[4] = o8[4] * a + f * x1[j].x; o8[5] = o8[5] * a + f * x1[j].y;
-              o8[6] = o8[6] * a + f * x1[j].z; o8[7] = o8[7] * a + f * x1[j].w;
+              o4[0] = o4[0] * a + f * x[j].x;
+              o4[1] = o4[1] * a + f * x[j].y;
+              o4[2] = o4[2] * a + f * x[j].z;
+              o4[3] = o4[3] * a + f * x[j].w;
               M = Mn;
             }
           }
         }
         if (ct == 0) tickets[b * p.n_kv + hkv] = 0u;
       }
-      // misc->last is reused by the next unit
+      // misc->last is reused by the next piece
       if (!consumer_sync(bar_csync, cph, abort_flag, &wsh->error)) break;
     }
     if (emit && g < G) {
       const size_t row = (size_t)b * p.n_heads + (size_t)hkv * G + g;
       if (p.partial) {
-        *reinterpret_cast<float2*>(p.part_ml + row * 2) = make_float2(M, Ls);
-        float4* dst = reinterpret_cast<float4*>(p.part_o + row * HD + d0);
-        dst[0] = make_float4(o8[0], o8[1], o8[2], o8[3]);
-        dst[1] = make_float4(o8[4], o8[5], o8[6], o8[7]);
+        if (d0 == 0) *reinterpret_cast<float2*>(p.part_ml + row * 2) = make_float2(M, Ls);
+        *reinterpret_cast<float4*>(p.part_o + row * HD + d0) =
+            make_float4(o4[0], o4[1], o4[2], o4[3]);
       } else {
         const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
-        uint4 v;
-        v.x = pack_half2(o8[0] * inv, o8[1] * inv);
-        v.y = pack_half2(o8[2] * inv, o8[3] * inv);
-        v.z = pack_half2(o8[4] * inv, o8[5] * inv);
-        v.w = pack_half2(o8[6] * inv, o8[7] * inv);
-        *reinterpret_cast<uint4*>(p.o + row * HD + d0) = v;
+        uint2 v;
+        v.x = pack_half2(o4[0] * inv, o4[1] * inv);
+        v.y = pack_half2(o4[2] * inv, o4[3] * inv);
+        *reinterpret_cast<uint2*>(p.o + row * HD + d0) = v;
       }
     }
   }
 }
 
 // ---------------- host side ----------------
-// Chunk policy: about `waves` units per CTA (one persistent CTA per SM), a
-// chunk at least min_chunk rows and at most max_chunk rows (longer chunks mean
-// fewer partials to merge; the queue balances ragged batches), and never more
-// than cap_per_sm units per SM.  Defaults from a sweep on B200 (config-3
-// ragged batch and config-2 single sequences).
+// Work-split policy.  When every (sequence, kv head) pair has at most
+// pair_max rows and there are no more pairs than SMs, each pair gets its own
+// CTA (no partials, lowest latency).  Otherwise each CTA's range holds at
+// least min_chunk (row, kv head) items, so small problems use fewer CTAs
+// instead of many tiny partials.
 struct Tuning {
-  uint32_t waves = 1;
-  uint32_t cap_per_sm = 64;
   uint32_t min_chunk = 256;
-  uint32_t max_chunk = 4096;
+  uint32_t pair_max = 512;
 };
 
 uint32_t env_u32(const char* name, uint32_t dflt) {
@@ -747,15 +843,15 @@ uint32_t env_u32(const char* name, uint32_t dflt) {
 const Tuning& tuning() {
   static Tuning t = [] {
     Tuning x;
-    x.waves = env_u32("NWD_DECODE_WAVES", x.waves);
-    x.cap_per_sm = env_u32("NWD_DECODE_UNITS_CAP_PER_SM", x.cap_per_sm);
-    x.min_chunk = (env_u32("NWD_DECODE_MIN_CHUNK", x.min_chunk) + TOK - 1) / TOK * TOK;
-    x.max_chunk = (env_u32("NWD_DECODE_MAX_CHUNK", x.max_chunk) + TOK - 1) / TOK * TOK;
-    if (x.max_chunk < x.min_chunk) x.max_chunk = x.min_chunk;
+    x.min_chunk = env_u32("NWD_DECODE_MIN_CHUNK", x.min_chunk);
+    x.pair_max = env_u32("NWD_DECODE_PAIR_MAX", x.pair_max);
     return x;
   }();
   return t;
 }
+
+// Partial slots: two per CTA (a range has at most a head and a tail piece).
+uint32_t slots_for(const nwd::DeviceInfo& di) { return 2u * (uint32_t)di.sm_count; }
 
 bool g_smem_set[64] = {false};
 
@@ -816,9 +912,8 @@ int launch(const Call& c) {
   if (st) return st;
   const Tuning& tu = tuning();
   const uint32_t grid_max = (uint32_t)di.sm_count;
-  const uint32_t units_cap = grid_max * tu.cap_per_sm;
   const uint32_t G = c.n_heads / c.n_kv;
-  const WsLayout lay = ws_layout(c.batch, c.n_kv, G, c.hd, units_cap);
+  const WsLayout lay = ws_layout(c.batch, c.n_kv, G, c.hd, slots_for(di));
   if (!c.ws) return fail(NWD_ERR_WORKSPACE, "%s: workspace is NULL", c.who);
   if (c.ws_bytes < lay.total)
     return fail(NWD_ERR_WORKSPACE, "%s: workspace of %zu bytes < %zu required", c.who, c.ws_bytes,
@@ -857,30 +952,32 @@ int launch(const Call& c) {
   p.tickets_off = lay.tickets_off;
   p.ml_off = lay.ml_off;
   p.o_off = lay.o_off;
-  p.max_units = lay.max_units;
+  p.nslots = lay.max_units;
   p.batch = c.batch;
   p.n_heads = c.n_heads;
   p.n_kv = c.n_kv;
   p.group = G;
+  if (!(c.scale >= 0.f) || isinf(c.scale))
+    return fail(NWD_ERR_INVALID, "%s: scale must be finite and >= 0 (0 = 1/sqrt(head_dim))", c.who);
   const float scale = c.scale != 0.f ? c.scale : 1.0f / sqrtf((float)c.hd);
   p.scale_log2 = scale * 1.4426950408889634f;
   p.append = c.append ? 1u : 0u;
   p.partial = c.partial ? 1u : 0u;
-  p.units_target = grid_max * tu.waves;
-  p.units_cap = units_cap;
   p.min_chunk = tu.min_chunk;
-  p.max_chunk = tu.max_chunk;
+  p.pair_max = tu.pair_max;
 
-  // grid: one CTA per SM, fewer when the plan cannot have that many units
+  // grid: one CTA per SM; for a single sequence (rows known here) one CTA per
+  // kv head when the sequence is short, else only as many CTAs as ranges of
+  // min_chunk items
   uint32_t grid = grid_max;
   if (!c.seq_len) {
-    const uint32_t L = c.single_len > 0 ? (uint32_t)c.single_len : 0u;
-    // upper bound on units: with C >= min_chunk
-    const uint64_t ub = (uint64_t)c.n_kv * (L / tu.min_chunk + 1);
-    if (ub < grid) grid = (uint32_t)ub;
-  } else {
-    const uint64_t ub = lay.max_units;
-    if (ub < grid) grid = (uint32_t)ub;
+    const uint64_t rows = (uint64_t)(c.single_len > 0 ? c.single_len : 0);
+    if (c.n_kv <= grid_max && rows <= tu.pair_max) {
+      grid = c.n_kv;
+    } else {
+      const uint64_t need = (c.n_kv * rows + tu.min_chunk - 1) / tu.min_chunk;
+      if (need < grid) grid = (uint32_t)need;
+    }
   }
   if (grid == 0) grid = 1;
   decode_kernel<<<grid, NTHR, SMEM_BYTES, (cudaStream_t)c.stream>>>(tmk, tmv, p);
@@ -903,8 +1000,8 @@ int nwd_attn_decode_workspace_size(uint32_t batch, uint32_t n_heads, uint32_t n_
   DeviceInfo di;
   st = current_device_info(&di);
   if (st) return st;
-  const uint32_t units_cap = (uint32_t)di.sm_count * tuning().cap_per_sm;
-  *bytes = ws_layout(batch ? batch : 1u, n_kv_heads, n_heads / n_kv_heads, head_dim, units_cap).total;
+  *bytes = ws_layout(batch ? batch : 1u, n_kv_heads, n_heads / n_kv_heads, head_dim,
+                     slots_for(di)).total;
   return ok();
 }
 

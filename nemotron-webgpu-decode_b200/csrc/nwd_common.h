@@ -38,19 +38,17 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // [256, +tickets)     uint32 per (sequence, kv head) merge tickets
 // then                float2 (m, l) per (unit, head) and float[hd] per (unit, head)
 struct WsHeader {
-  uint32_t error;       // NWD_DEVERR_* bits
-  uint32_t next_unit;   // dynamic scheduler: next unit to hand out
-  uint32_t done_ctas;   // CTAs that found the queue empty
-  uint32_t pad[61];
+  uint32_t error;  // NWD_DEVERR_* bits
+  uint32_t pad[63];
 };
 static_assert(sizeof(WsHeader) == 256, "header is 256 bytes");
 
 struct WsLayout {
   size_t tickets_off, ml_off, o_off, total;
-  uint32_t max_units;
+  uint32_t max_units;  // partial slots
 };
-// Layout for `batch` sequences, kv heads n_kv, group g, on a device with
-// `units_cap` units at most (see decode.cu for the chunk policy).
-WsLayout ws_layout(uint32_t batch, uint32_t n_kv, uint32_t group, uint32_t hd, uint32_t units_cap);
+// Layout for `batch` sequences, kv heads n_kv, group g, with `slots` partial
+// slots (decode.cu: two per CTA).
+WsLayout ws_layout(uint32_t batch, uint32_t n_kv, uint32_t group, uint32_t hd, uint32_t slots);
 
 }  // namespace nwd
