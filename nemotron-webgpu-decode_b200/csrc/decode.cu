@@ -48,12 +48,9 @@ using nwd::WsHeader;
 
 constexpr int HD = 128;                  // head_dim supported by the tiles
 constexpr int WPG = 4;                   // consumer warps per group (16 rows each)
-constexpr int NGRP = 2;                  // consumer groups, taking alternate stages
-constexpr int NCW = WPG * NGRP;          // consumer warps
 constexpr int TOK = 16 * WPG;            // rows per stage
 constexpr int NST = 5;                   // pipeline stages
 constexpr int GMAX = 8;                  // query heads per kv head (mma N)
-constexpr int NTHR = (NCW + 1) * 32;     // + producer warp
 constexpr int KV_BYTES = TOK * HD * 2;   // one K (or V) stage: 16 KiB
 constexpr int Q_BYTES = GMAX * HD * 2;   // query rows of one kv head
 constexpr int MAXB = 4096;               // sequences per launch
@@ -96,19 +93,30 @@ constexpr int OFF_K = 0;
 constexpr int OFF_V = OFF_K + NST * KV_BYTES;
 constexpr int OFF_Q = OFF_V + NST * KV_BYTES;
 constexpr int OFF_MRG = OFF_Q + NST * Q_BYTES;
-constexpr int MRG_FLOATS = NCW * GMAX * (HD + 2);
-constexpr int OFF_PFX = OFF_MRG + MRG_FLOATS * 4;
-constexpr int OFF_HDR = OFF_PFX + ((MAXB + 1) * 4 + 15) / 16 * 16;
-constexpr int OFF_BAR = OFF_HDR + NST * (int)sizeof(StageHdr);
-constexpr int OFF_MISC = OFF_BAR + 2 * NST * 8 + 8;  // + consumer-sync barrier
-constexpr int SMEM_USED = OFF_MISC + 64;
-constexpr int SMEM_BYTES = SMEM_USED + 1024;  // slack for manual 1024-byte alignment
-static_assert(SMEM_BYTES <= 227 * 1024, "exceeds the 227 KiB per-CTA shared memory of sm_100");
+
+// Configuration by number of consumer groups NG: one group of four warps, or
+// two groups taking alternate stages (two warps per SM sub-partition, which
+// hides the MMA / shuffle latency of the softmax chain when streaming).
+template <int NG>
+struct Cfg {
+  static constexpr int NCW = WPG * NG;                  // consumer warps
+  static constexpr int NTHR = (NCW + 1) * 32;           // + producer warp
+  static constexpr int MRG_FLOATS = NCW * GMAX * (HD + 2);
+  static constexpr int OFF_PFX = OFF_MRG + MRG_FLOATS * 4;
+  static constexpr int OFF_HDR = OFF_PFX + ((MAXB + 1) * 4 + 15) / 16 * 16;
+  static constexpr int OFF_BAR = OFF_HDR + NST * (int)sizeof(StageHdr);
+  static constexpr int OFF_MISC = OFF_BAR + 2 * NST * 8 + 8;  // + consumer-sync barrier
+  static constexpr int SMEM_USED = OFF_MISC + 64;
+  static constexpr int SMEM_BYTES = SMEM_USED + 1024;  // slack for manual 1024-byte alignment
+  static constexpr int DPT = GMAX * HD / (NCW * 32);   // epilogue dims per thread (8 or 4)
+  static_assert(SMEM_BYTES <= 227 * 1024, "exceeds the 227 KiB per-CTA shared memory of sm_100");
+  static_assert(NG == 1 || NG == 2, "one or two consumer groups");
+};
 
 struct Misc {
   int32_t abort;
   int32_t last;
-  uint32_t warp_sum[NTHR / 32];
+  uint32_t warp_sum[10];
   uint32_t max_rows;
   uint64_t total_rows;
 };
@@ -261,6 +269,7 @@ __device__ __forceinline__ uint32_t cdiv(uint64_t a, uint64_t b) { return (uint3
 
 // Block-wide exclusive scan of per-thread values; returns this thread's
 // offset, writes the grand total to *total (all threads see it after return).
+template <int NTHR>
 __device__ uint32_t block_scan(uint32_t v, Misc* misc, uint32_t* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t x = v;
@@ -301,19 +310,22 @@ __device__ __forceinline__ uint64_t udiv64(uint64_t a, uint64_t b) {
   return a / b;
 }
 
-__global__ void __launch_bounds__(NTHR, 1)
+template <int NG>
+__global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
     decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                   const __grid_constant__ Params p) {
+  using C = Cfg<NG>;
+  constexpr int NCW = C::NCW, NTHR = C::NTHR, NGRP = NG;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sbase = smem_u32(smem);
-  uint32_t* S = reinterpret_cast<uint32_t*>(smem + OFF_PFX);  // row prefix over sequences
-  StageHdr* hdr = reinterpret_cast<StageHdr*>(smem + OFF_HDR);
-  Misc* misc = reinterpret_cast<Misc*>(smem + OFF_MISC);
+  uint32_t* S = reinterpret_cast<uint32_t*>(smem + C::OFF_PFX);  // row prefix over sequences
+  StageHdr* hdr = reinterpret_cast<StageHdr*>(smem + C::OFF_HDR);
+  Misc* misc = reinterpret_cast<Misc*>(smem + C::OFF_MISC);
   volatile int32_t* abort_flag = &misc->abort;
-  const uint32_t bar_full = sbase + OFF_BAR;            // + 8*s
-  const uint32_t bar_empty = sbase + OFF_BAR + 8 * NST; // + 8*s
-  const uint32_t bar_csync = sbase + OFF_BAR + 16 * NST;
+  const uint32_t bar_full = sbase + C::OFF_BAR;            // + 8*s
+  const uint32_t bar_empty = sbase + C::OFF_BAR + 8 * NST; // + 8*s
+  const uint32_t bar_csync = sbase + C::OFF_BAR + 16 * NST;
   WsHeader* wsh = reinterpret_cast<WsHeader*>(p.ws);
   uint32_t* tickets = reinterpret_cast<uint32_t*>(p.ws + p.tickets_off);
   float* ws_ml = reinterpret_cast<float*>(p.ws + p.ml_off);
@@ -352,7 +364,7 @@ __global__ void __launch_bounds__(NTHR, 1)
               (unsigned long long)rows_local);
   if (max_local) atomicMax(&misc->max_rows, max_local);
   uint32_t total32;
-  uint32_t run = block_scan((uint32_t)rows_local, misc, &total32);  // syncs: sums final
+  uint32_t run = block_scan<NTHR>((uint32_t)rows_local, misc, &total32);  // syncs: sums final
   if (misc->total_rows >= (1ull << 32)) {
     // more than 2^32 rows in one call: refuse (uniform across the block)
     if (tid == 0 && blockIdx.x == 0) atomicOr(&wsh->error, NWD_DEVERR_ROW_RANGE);
@@ -429,7 +441,7 @@ __global__ void __launch_bounds__(NTHR, 1)
         __syncwarp();
       }
       const uint32_t nreal = cdiv(t1 - t0, TOK);
-      const uint32_t nstages = (nreal + 1u) & ~1u;
+      const uint32_t nstages = (nreal + NGRP - 1u) / NGRP * NGRP;
       for (uint32_t s = 0; s < nstages && !aborted; s++) {
         if (!warp_wait(bar_empty + 8 * slot, phase ^ 1u, abort_flag, &wsh->error)) {
           aborted = true;
@@ -441,7 +453,7 @@ __global__ void __launch_bounds__(NTHR, 1)
           h.hkv = (int32_t)hkv;
           h.t0 = (int32_t)(t0 + s * TOK);
           h.ntok = s < nreal ? (int32_t)min((uint32_t)TOK, t1 - (t0 + s * TOK)) : 0;
-          h.flags = (s < 2 ? F_FIRST : 0) | (s + 2 >= nstages ? F_LAST : 0) |
+          h.flags = (s < (uint32_t)NGRP ? F_FIRST : 0) | (s + NGRP >= nstages ? F_LAST : 0) |
                     (complete ? F_COMPLETE : 0);
           h.slot = pslot;
           h.f = f;
@@ -449,7 +461,7 @@ __global__ void __launch_bounds__(NTHR, 1)
           hdr[slot] = h;
           const uint32_t fb = bar_full + 8 * slot;
           if (h.ntok > 0) {
-            const uint32_t qbytes = (s < 2) ? G * HD * 2 : 0u;
+            const uint32_t qbytes = (s < (uint32_t)NGRP) ? G * HD * 2 : 0u;
             mbar_arrive_tx(fb, 2 * KV_BYTES + qbytes);
             const int row = (int)(off + (int64_t)h.t0);
             tma_load_4d(sbase + OFF_K + slot * KV_BYTES, &tmk, fb, 0, 0, (int)hkv, row, policy);
@@ -565,7 +577,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     // is odd).  A parity wait cannot tell phase k from phase k+2, so first
     // wait until the slot's previous use (the other group's stage) has been
     // released: then the full barrier is at most one phase behind this wait.
-    if (!warp_wait(bar_empty + 8 * slot, phase ^ 1u, abort_flag, &wsh->error)) break;
+    if (NGRP > 1 && !warp_wait(bar_empty + 8 * slot, phase ^ 1u, abort_flag, &wsh->error)) break;
     if (!warp_wait(bar_full + 8 * slot, phase, abort_flag, &wsh->error)) break;
     const StageHdr h = hdr[slot];
     if (h.flags & F_TERM) break;
@@ -722,23 +734,31 @@ __global__ void __launch_bounds__(NTHR, 1)
       }
     }
     if (!consumer_sync(bar_csync, cph, abort_flag, &wsh->error)) break;
-    // 256 threads: head g, dims d0 .. d0+3
+    // NCW*32 threads: head g, dims d0 .. d0+DPT-1
+    constexpr int DPT = C::DPT, NV = DPT / 4;
     const uint32_t ct = warp * 32 + lane;
-    const uint32_t g = ct >> 5, d0 = (ct & 31) * 4;
+    const uint32_t g = ct / (HD / DPT), d0 = (ct % (HD / DPT)) * DPT;
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < NCW; w++) M = fmaxf(M, mrg_m[w * GMAX + g]);
-    float Ls = 0.f, o4[4] = {0.f, 0.f, 0.f, 0.f};
+    float Ls = 0.f;
+    float4 o4[NV];
+#pragma unroll
+    for (int j = 0; j < NV; j++) o4[j] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int w = 0; w < NCW; w++) {
       const float mw = mrg_m[w * GMAX + g];
       const float f = mw == -INFINITY ? 0.f : ex2(mw - M);
       Ls += f * mrg_l[w * GMAX + g];
-      const float4 a = *reinterpret_cast<const float4*>(mrg_acc + ((size_t)w * GMAX + g) * HD + d0);
-      o4[0] += f * a.x;
-      o4[1] += f * a.y;
-      o4[2] += f * a.z;
-      o4[3] += f * a.w;
+      const float4* a = reinterpret_cast<const float4*>(mrg_acc + ((size_t)w * GMAX + g) * HD + d0);
+#pragma unroll
+      for (int j = 0; j < NV; j++) {
+        const float4 x = a[j];
+        o4[j].x += f * x.x;
+        o4[j].y += f * x.y;
+        o4[j].z += f * x.z;
+        o4[j].w += f * x.w;
+      }
     }
     if (!consumer_sync(bar_csync, cph, abort_flag, &wsh->error)) break;  // scratch free again
 
@@ -750,7 +770,9 @@ __global__ void __launch_bounds__(NTHR, 1)
       if (g < G) {
         const size_t sl = (size_t)h.slot * G + g;
         if (d0 == 0) *reinterpret_cast<float2*>(ws_ml + sl * 2) = make_float2(M, Ls);
-        *reinterpret_cast<float4*>(ws_o + sl * HD + d0) = make_float4(o4[0], o4[1], o4[2], o4[3]);
+        float4* dst = reinterpret_cast<float4*>(ws_o + sl * HD + d0);
+#pragma unroll
+        for (int j = 0; j < NV; j++) dst[j] = o4[j];
       }
       __threadfence();
       if (!consumer_sync(bar_csync, cph, abort_flag, &wsh->error)) break;
@@ -768,10 +790,10 @@ __global__ void __launch_bounds__(NTHR, 1)
           M = -INFINITY;
           Ls = 0.f;
 #pragma unroll
-          for (int j = 0; j < 4; j++) o4[j] = 0.f;
+          for (int j = 0; j < NV; j++) o4[j] = make_float4(0.f, 0.f, 0.f, 0.f);
           for (int32_t c0 = h.f; c0 <= h.l; c0 += 8) {
             float2 ml[8];
-            float4 x[8];
+            float4 x[8][NV];
 #pragma unroll
             for (int j = 0; j < 8; j++) {
               const int32_t c = c0 + j;
@@ -779,10 +801,13 @@ __global__ void __launch_bounds__(NTHR, 1)
                 // CTA f holds the pair's head in its tail slot; later CTAs in their head slot
                 const size_t sl = (size_t)(2 * c + (c == h.f ? 1 : 0)) * G + g;
                 ml[j] = __ldcg(reinterpret_cast<const float2*>(ws_ml + sl * 2));
-                x[j] = __ldcg(reinterpret_cast<const float4*>(ws_o + sl * HD + d0));
+                const float4* src = reinterpret_cast<const float4*>(ws_o + sl * HD + d0);
+#pragma unroll
+                for (int v = 0; v < NV; v++) x[j][v] = __ldcg(src + v);
               } else {
                 ml[j] = make_float2(-INFINITY, 0.f);
-                x[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int v = 0; v < NV; v++) x[j][v] = make_float4(0.f, 0.f, 0.f, 0.f);
               }
             }
 #pragma unroll
@@ -792,10 +817,13 @@ __global__ void __launch_bounds__(NTHR, 1)
               const float a = ex2(M - Mn);  // 0 while M is -inf
               const float f = ex2(ml[j].x - Mn);
               Ls = Ls * a + f * ml[j].y;
-              o4[0] = o4[0] * a + f * x[j].x;
-              o4[1] = o4[1] * a + f * x[j].y;
-              o4[2] = o4[2] * a + f * x[j].z;
-              o4[3] = o4[3] * a + f * x[j].w;
+#pragma unroll
+              for (int v = 0; v < NV; v++) {
+                o4[v].x = o4[v].x * a + f * x[j][v].x;
+                o4[v].y = o4[v].y * a + f * x[j][v].y;
+                o4[v].z = o4[v].z * a + f * x[j][v].z;
+                o4[v].w = o4[v].w * a + f * x[j][v].w;
+              }
               M = Mn;
             }
           }
@@ -809,14 +837,18 @@ __global__ void __launch_bounds__(NTHR, 1)
       const size_t row = (size_t)b * p.n_heads + (size_t)hkv * G + g;
       if (p.partial) {
         if (d0 == 0) *reinterpret_cast<float2*>(p.part_ml + row * 2) = make_float2(M, Ls);
-        *reinterpret_cast<float4*>(p.part_o + row * HD + d0) =
-            make_float4(o4[0], o4[1], o4[2], o4[3]);
+        float4* dst = reinterpret_cast<float4*>(p.part_o + row * HD + d0);
+#pragma unroll
+        for (int j = 0; j < NV; j++) dst[j] = o4[j];
       } else {
         const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
-        uint2 v;
-        v.x = pack_half2(o4[0] * inv, o4[1] * inv);
-        v.y = pack_half2(o4[2] * inv, o4[3] * inv);
-        *reinterpret_cast<uint2*>(p.o + row * HD + d0) = v;
+#pragma unroll
+        for (int j = 0; j < NV; j++) {
+          uint2 v;
+          v.x = pack_half2(o4[j].x * inv, o4[j].y * inv);
+          v.y = pack_half2(o4[j].z * inv, o4[j].w * inv);
+          *reinterpret_cast<uint2*>(p.o + row * HD + d0 + 4 * j) = v;
+        }
       }
     }
   }
@@ -831,6 +863,8 @@ __global__ void __launch_bounds__(NTHR, 1)
 struct Tuning {
   uint32_t min_chunk = 256;
   uint32_t pair_max = 512;
+  uint32_t groups = 0;  // consumer groups: 0 = by problem size, else 1 or 2
+  uint32_t two_group_rows = 8192;  // single sequence: two groups from this many rows
 };
 
 uint32_t env_u32(const char* name, uint32_t dflt) {
@@ -845,6 +879,9 @@ const Tuning& tuning() {
     Tuning x;
     x.min_chunk = env_u32("NWD_DECODE_MIN_CHUNK", x.min_chunk);
     x.pair_max = env_u32("NWD_DECODE_PAIR_MAX", x.pair_max);
+    x.groups = env_u32("NWD_DECODE_GROUPS", x.groups);
+    if (x.groups > 2) x.groups = 2;
+    x.two_group_rows = env_u32("NWD_DECODE_TWO_GROUP_ROWS", x.two_group_rows);
     return x;
   }();
   return t;
@@ -853,7 +890,7 @@ const Tuning& tuning() {
 // Partial slots: two per CTA (a range has at most a head and a tail piece).
 uint32_t slots_for(const nwd::DeviceInfo& di) { return 2u * (uint32_t)di.sm_count; }
 
-bool g_smem_set[64] = {false};
+bool g_smem_set[64][3] = {};
 
 struct Call {
   const uint16_t* q;
@@ -922,12 +959,6 @@ int launch(const Call& c) {
     return fail(NWD_ERR_WORKSPACE, "%s: workspace must be 256-byte aligned", c.who);
   if (c.batch == 0) return ok();
 
-  if (!g_smem_set[di.device]) {
-    cudaError_t e =
-        cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode_kernel)");
-    g_smem_set[di.device] = true;
-  }
   CUtensorMap tmk, tmv;
   st = kv_tensor_map(&tmk, c.k_pool, c.pool_rows, c.n_kv, c.hd, TOK);
   if (st) return st;
@@ -980,7 +1011,24 @@ int launch(const Call& c) {
     }
   }
   if (grid == 0) grid = 1;
-  decode_kernel<<<grid, NTHR, SMEM_BYTES, (cudaStream_t)c.stream>>>(tmk, tmv, p);
+  // Consumer groups: two (latency hiding) for batched calls and long single
+  // sequences, one for short single sequences (its epilogue is shorter).
+  uint32_t ng = tu.groups;
+  if (ng == 0) ng = (c.seq_len || (uint64_t)c.single_len >= tu.two_group_rows) ? 2u : 1u;
+  if (!g_smem_set[di.device][ng]) {
+    cudaError_t e = ng == 2 ? cudaFuncSetAttribute(decode_kernel<2>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   Cfg<2>::SMEM_BYTES)
+                            : cudaFuncSetAttribute(decode_kernel<1>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   Cfg<1>::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode_kernel)");
+    g_smem_set[di.device][ng] = true;
+  }
+  if (ng == 2)
+    decode_kernel<2><<<grid, Cfg<2>::NTHR, Cfg<2>::SMEM_BYTES, (cudaStream_t)c.stream>>>(tmk, tmv, p);
+  else
+    decode_kernel<1><<<grid, Cfg<1>::NTHR, Cfg<1>::SMEM_BYTES, (cudaStream_t)c.stream>>>(tmk, tmv, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, c.who);
   return ok();
