@@ -1,0 +1,208 @@
+// N-API addon over the nwd C ABI: the binding engine/runtime.js would load in
+// place of the WGSL pipelines of its attention layers (engine/runtime.js:101-102,
+// :331-333, :389-391).  Built only where Node's headers exist (node-gyp /
+// cmake-js with node_api.h); this repository's build does not compile it.
+//
+// JS surface (mirrors the WGSL Params of the two replaced kernels):
+//   nwd.kvAppend(src, cache, {seq, n_kv, hd, cap})
+//       kernels/kv_append.wgsl Params {seq, n_kv, hd} (+ cap, the row capacity)
+//   nwd.attention(q, kCache, vCache, o, {n_heads, n_kv_heads, head_dim, seq, cap})
+//       kernels/sparse_attn.wgsl Params {n_heads, n_kv_heads, head_dim, seq}
+//   nwd.kvAppendAttention(q, kNew, vNew, kCache, vCache, o, {..., seq, cap})
+//       the engine step of runtime.js:389-391 in one launch
+//   nwd.alloc(bytes) / nwd.free(buf) / nwd.upload(buf, typedArray) / nwd.download(buf, typedArray)
+// Buffers are napi_external wrappers of device pointers.  A non-zero status
+// throws Error(nwd_last_error()), as runtime.js throws on errors (:448, :484).
+#include <cuda_runtime.h>
+#include <node_api.h>
+
+#include <cstdint>
+#include <string>
+
+#include "nwd.h"
+
+namespace {
+
+struct DevBuf {
+  void* ptr;
+  size_t bytes;
+};
+
+napi_value throw_status(napi_env env, int status) {
+  std::string msg = std::string(nwd_status_name(status)) + ": " + nwd_last_error();
+  napi_throw_error(env, nullptr, msg.c_str());
+  return nullptr;
+}
+
+void finalize_buf(napi_env, void* data, void*) {
+  auto* b = static_cast<DevBuf*>(data);
+  if (b->ptr) cudaFree(b->ptr);
+  delete b;
+}
+
+DevBuf* get_buf(napi_env env, napi_value v) {
+  void* data = nullptr;
+  if (napi_get_value_external(env, v, &data) != napi_ok) {
+    napi_throw_type_error(env, nullptr, "expected a device buffer from nwd.alloc");
+    return nullptr;
+  }
+  return static_cast<DevBuf*>(data);
+}
+
+uint32_t get_u32(napi_env env, napi_value obj, const char* key, uint32_t dflt = 0,
+                 bool required = true) {
+  bool has = false;
+  napi_has_named_property(env, obj, key, &has);
+  if (!has) {
+    if (required) napi_throw_type_error(env, nullptr, (std::string("missing ") + key).c_str());
+    return dflt;
+  }
+  napi_value v;
+  napi_get_named_property(env, obj, key, &v);
+  uint32_t out = dflt;
+  napi_get_value_uint32(env, v, &out);
+  return out;
+}
+
+// Per-engine scratch: one workspace per attention shape, zeroed once.
+struct Workspace {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  uint32_t nh = 0, nkv = 0, hd = 0;
+};
+Workspace g_ws;
+
+int ensure_ws(uint32_t nh, uint32_t nkv, uint32_t hd) {
+  if (g_ws.ptr && g_ws.nh == nh && g_ws.nkv == nkv && g_ws.hd == hd) return NWD_OK;
+  size_t bytes = 0;
+  int st = nwd_attn_decode_workspace_size(1, nh, nkv, hd, &bytes);
+  if (st) return st;
+  if (g_ws.ptr) cudaFree(g_ws.ptr);
+  g_ws = Workspace{};
+  if (cudaMalloc(&g_ws.ptr, bytes) != cudaSuccess) return NWD_ERR_CUDA;
+  st = nwd_workspace_init(g_ws.ptr, bytes, nullptr);
+  if (st) return st;
+  g_ws.bytes = bytes;
+  g_ws.nh = nh;
+  g_ws.nkv = nkv;
+  g_ws.hd = hd;
+  return NWD_OK;
+}
+
+napi_value Alloc(napi_env env, napi_callback_info info) {
+  size_t argc = 1;
+  napi_value argv[1];
+  napi_get_cb_info(env, info, &argc, argv, nullptr, nullptr);
+  int64_t bytes = 0;
+  napi_get_value_int64(env, argv[0], &bytes);
+  auto* b = new DevBuf{nullptr, (size_t)bytes};
+  if (cudaMalloc(&b->ptr, b->bytes) != cudaSuccess || cudaMemset(b->ptr, 0, b->bytes) != cudaSuccess) {
+    delete b;
+    napi_throw_error(env, nullptr, "cudaMalloc failed");
+    return nullptr;
+  }
+  napi_value out;
+  napi_create_external(env, b, finalize_buf, nullptr, &out);
+  return out;
+}
+
+napi_value Copy(napi_env env, napi_callback_info info, bool upload) {
+  size_t argc = 2;
+  napi_value argv[2];
+  napi_get_cb_info(env, info, &argc, argv, nullptr, nullptr);
+  DevBuf* b = get_buf(env, argv[0]);
+  if (!b) return nullptr;
+  napi_typedarray_type type;
+  size_t length;
+  void* data;
+  napi_value ab;
+  size_t offset;
+  napi_get_typedarray_info(env, argv[1], &type, &length, &data, &ab, &offset);
+  size_t elem = (type == napi_uint16_array || type == napi_int16_array) ? 2
+                : (type == napi_uint8_array || type == napi_int8_array)   ? 1
+                                                                           : 4;
+  size_t bytes = length * elem;
+  if (bytes > b->bytes) {
+    napi_throw_range_error(env, nullptr, "typed array larger than the device buffer");
+    return nullptr;
+  }
+  cudaError_t e = upload ? cudaMemcpy(b->ptr, data, bytes, cudaMemcpyHostToDevice)
+                         : cudaMemcpy(data, b->ptr, bytes, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) {
+    napi_throw_error(env, nullptr, cudaGetErrorString(e));
+    return nullptr;
+  }
+  return nullptr;
+}
+napi_value Upload(napi_env env, napi_callback_info info) { return Copy(env, info, true); }
+napi_value Download(napi_env env, napi_callback_info info) { return Copy(env, info, false); }
+
+napi_value KvAppend(napi_env env, napi_callback_info info) {
+  size_t argc = 3;
+  napi_value argv[3];
+  napi_get_cb_info(env, info, &argc, argv, nullptr, nullptr);
+  DevBuf* src = get_buf(env, argv[0]);
+  DevBuf* cache = get_buf(env, argv[1]);
+  if (!src || !cache) return nullptr;
+  uint32_t seq = get_u32(env, argv[2], "seq"), n_kv = get_u32(env, argv[2], "n_kv"),
+           hd = get_u32(env, argv[2], "hd");
+  uint32_t cap = get_u32(env, argv[2], "cap", (uint32_t)(cache->bytes / (2ull * n_kv * hd)), false);
+  int st = nwd_kv_append((const uint16_t*)src->ptr, (uint16_t*)cache->ptr, seq, n_kv, hd, cap,
+                         nullptr);
+  return st ? throw_status(env, st) : nullptr;
+}
+
+napi_value Attention(napi_env env, napi_callback_info info) {
+  size_t argc = 5;
+  napi_value argv[5];
+  napi_get_cb_info(env, info, &argc, argv, nullptr, nullptr);
+  DevBuf *q = get_buf(env, argv[0]), *k = get_buf(env, argv[1]), *v = get_buf(env, argv[2]),
+         *o = get_buf(env, argv[3]);
+  if (!q || !k || !v || !o) return nullptr;
+  uint32_t nh = get_u32(env, argv[4], "n_heads"), nkv = get_u32(env, argv[4], "n_kv_heads"),
+           hd = get_u32(env, argv[4], "head_dim"), seq = get_u32(env, argv[4], "seq");
+  uint32_t cap = get_u32(env, argv[4], "cap", (uint32_t)(k->bytes / (2ull * nkv * hd)), false);
+  int st = ensure_ws(nh, nkv, hd);
+  if (!st)
+    st = nwd_attn_decode((const uint16_t*)q->ptr, (const uint16_t*)k->ptr,
+                         (const uint16_t*)v->ptr, (uint16_t*)o->ptr, nh, nkv, hd, seq, cap, 0.0f,
+                         g_ws.ptr, g_ws.bytes, nullptr);
+  return st ? throw_status(env, st) : nullptr;
+}
+
+napi_value KvAppendAttention(napi_env env, napi_callback_info info) {
+  size_t argc = 7;
+  napi_value argv[7];
+  napi_get_cb_info(env, info, &argc, argv, nullptr, nullptr);
+  DevBuf *q = get_buf(env, argv[0]), *kn = get_buf(env, argv[1]), *vn = get_buf(env, argv[2]),
+         *kc = get_buf(env, argv[3]), *vc = get_buf(env, argv[4]), *o = get_buf(env, argv[5]);
+  if (!q || !kn || !vn || !kc || !vc || !o) return nullptr;
+  uint32_t nh = get_u32(env, argv[6], "n_heads"), nkv = get_u32(env, argv[6], "n_kv_heads"),
+           hd = get_u32(env, argv[6], "head_dim"), seq = get_u32(env, argv[6], "seq");
+  uint32_t cap = get_u32(env, argv[6], "cap", (uint32_t)(kc->bytes / (2ull * nkv * hd)), false);
+  int st = ensure_ws(nh, nkv, hd);
+  if (!st)
+    st = nwd_kv_append_attn_decode((const uint16_t*)q->ptr, (const uint16_t*)kn->ptr,
+                                   (const uint16_t*)vn->ptr, (uint16_t*)kc->ptr,
+                                   (uint16_t*)vc->ptr, (uint16_t*)o->ptr, nh, nkv, hd, seq, cap,
+                                   0.0f, g_ws.ptr, g_ws.bytes, nullptr);
+  return st ? throw_status(env, st) : nullptr;
+}
+
+napi_value Init(napi_env env, napi_value exports) {
+  napi_property_descriptor props[] = {
+      {"alloc", nullptr, Alloc, nullptr, nullptr, nullptr, napi_default, nullptr},
+      {"upload", nullptr, Upload, nullptr, nullptr, nullptr, napi_default, nullptr},
+      {"download", nullptr, Download, nullptr, nullptr, nullptr, napi_default, nullptr},
+      {"kvAppend", nullptr, KvAppend, nullptr, nullptr, nullptr, napi_default, nullptr},
+      {"attention", nullptr, Attention, nullptr, nullptr, nullptr, napi_default, nullptr},
+      {"kvAppendAttention", nullptr, KvAppendAttention, nullptr, nullptr, nullptr, napi_default,
+       nullptr},
+  };
+  napi_define_properties(env, exports, sizeof(props) / sizeof(props[0]), props);
+  return exports;
+}
+
+}  // namespace
+
+NAPI_MODULE(NODE_GYP_MODULE_NAME, Init)

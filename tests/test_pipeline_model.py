@@ -1,0 +1,247 @@
+"""CPU models of the decode kernel's work split and stage-ring protocol.
+
+csrc/decode.cu plans its work per CTA (stream-K ranges cut into pieces at
+(sequence, kv head) pair boundaries, or one CTA per pair for small problems)
+and runs a producer warp and NG consumer groups over a ring of NST mbarrier-
+guarded stages.  Neither can be inspected on the GPU, so both are restated
+here and checked:
+
+* the planner: pieces partition every pair exactly, the ticket count of a
+  pair (l - f + 1) equals the pieces that exist, and no CTA reuses a partial
+  slot;
+* the protocol, with PTX mbarrier semantics (a parity wait only compares the
+  current phase's parity): every consumer group consumes exactly its own
+  stages in order under random timing.  Without the "wait for the slot's
+  previous release" gate the two-group ring consumes a stale stage; the model
+  shows both.
+"""
+from __future__ import annotations
+
+import random
+
+import numpy as np
+import pytest
+
+TOK, NST, WPG = 64, 5, 4
+
+
+# ---------------------------------------------------------------- planner
+
+def plan(lens, nkv, grid, min_chunk=256, pair_max=512):
+    """Pieces (cta, b, hkv, t0, t1, complete, f, l) as decode_kernel walks them."""
+    B = len(lens)
+    S = [0]
+    for L in lens:
+        S.append(S[-1] + L)
+    T = nkv * S[B]
+    pair_mode = B * nkv <= grid and max(lens) <= pair_max
+    W = max((T + grid - 1) // grid, min_chunk)
+    out = []
+    for i in range(grid):
+        if pair_mode:
+            if i < B * nkv:
+                b, h = divmod(i, nkv)
+                if lens[b]:
+                    out.append((i, b, h, 0, lens[b], True, i, i))
+            continue
+        x0, x1 = min(T, i * W), min(T, i * W + W)
+        if x0 >= x1:
+            continue
+        y = x0 // nkv
+        b = max(j for j in range(B) if S[j] <= y)
+        L = S[b + 1] - S[b]
+        r = x0 - nkv * S[b]
+        h, t0 = divmod(r, L)
+        pstart, f, x = x0 - t0, (x0 - t0) // W, x0
+        while x < x1:
+            ln = min(L - t0, x1 - x)
+            t1 = t0 + ln
+            l = i if t1 == L else (pstart + L - 1) // W
+            out.append((i, b, h, t0, t1, t0 == 0 and t1 == L, f, l))
+            x += ln
+            if x >= x1:
+                break
+            pstart, t0, f = x, 0, i
+            h += 1
+            if h == nkv:
+                h = 0
+                b += 1
+                while b + 1 < B and S[b + 1] == S[b]:
+                    b += 1
+                L = S[b + 1] - S[b]
+    return out, S
+
+
+def check_plan(lens, nkv, grid, **kw):
+    pieces, S = plan(lens, nkv, grid, **kw)
+    cover, slots = {}, set()
+    for (i, b, h, t0, t1, comp, f, l) in pieces:
+        assert 0 <= t0 < t1 <= S[b + 1] - S[b]
+        cover.setdefault((b, h), []).append((t0, t1, i, f, l))
+        if not comp:
+            s = 2 * i + (0 if t0 > 0 else 1)
+            assert s not in slots, "partial slot reused"
+            slots.add(s)
+    for b, L in enumerate(lens):
+        for h in range(nkv):
+            if L == 0:
+                assert (b, h) not in cover
+                continue
+            ps = sorted(cover[(b, h)])
+            assert ps[0][0] == 0 and ps[-1][1] == L
+            assert all(a[1] == c[0] for a, c in zip(ps, ps[1:]))
+            f, l = ps[0][3], ps[0][4]
+            assert all(p[3] == f and p[4] == l for p in ps)
+            if len(ps) > 1:
+                assert l - f + 1 == len(ps)
+                assert [p[2] for p in ps] == list(range(f, l + 1))
+    return pieces
+
+
+def test_planner_bench_shapes():
+    check_plan([262144], 8, 148)
+    check_plan([32768], 8, 148)
+    check_plan([151], 8, 8)  # engine trace: one CTA per kv head
+    lens = np.random.default_rng(3).integers(512, 8193, 256) + 1
+    pieces = check_plan([int(x) for x in lens], 8, 148)
+    per_cta = {}
+    for p in pieces:
+        per_cta.setdefault(p[0], 0)
+        per_cta[p[0]] += p[4] - p[3]
+    # stream-K: every CTA streams the same rows (the last one the remainder)
+    sizes = sorted(per_cta.values())
+    assert sizes[-1] - sizes[1] <= 0
+
+
+def test_planner_random_shapes():
+    rng = np.random.default_rng(0)
+    for _ in range(200):
+        B = int(rng.integers(1, 200))
+        hi = int(rng.choice([3, 100, 5000, 70000]))
+        lens = [int(x) for x in rng.integers(0, hi, B)]
+        if sum(lens) == 0:
+            continue
+        check_plan(lens, int(rng.choice([1, 2, 8])), int(rng.choice([8, 37, 148])),
+                   min_chunk=int(rng.choice([64, 256])))
+
+
+# ---------------------------------------------------------------- protocol
+
+class Bar:
+    """mbarrier: arrival count, transaction bytes, phase; parity waits."""
+
+    def __init__(self, count):
+        self.count, self.pending, self.tx, self.phase = count, count, 0, 0
+
+    def arrive(self, tx=0):
+        self.tx += tx
+        self.pending -= 1
+        self._step()
+
+    def complete_tx(self, n):
+        self.tx -= n
+        self._step()
+
+    def _step(self):
+        if self.pending == 0 and self.tx == 0:
+            self.phase += 1
+            self.pending = self.count
+
+    def passed(self, parity):  # mbarrier.try_wait.parity
+        return (self.phase & 1) != parity
+
+
+def simulate(piece_stages, ngroups, gate, seed):
+    rng = random.Random(seed)
+    full = [Bar(1) for _ in range(NST)]
+    empty = [Bar(WPG) for _ in range(NST)]
+    csync = Bar(WPG * ngroups * 32)
+    prog = []
+    for k, n in enumerate(piece_stages):
+        n2 = -(-n // ngroups) * ngroups
+        syncs = 2 + 3 * (k % 2)  # complete pieces: 2 syncs; partial pieces: 5
+        for s in range(n2):
+            prog.append((s < n, s + ngroups >= n2, syncs))
+    prog += [None] * ngroups
+    hdr = [None] * NST
+    flight = []
+
+    def producer():
+        slot = phase = 0
+        for c, op in enumerate(prog):
+            while not empty[slot].passed(phase ^ 1):
+                yield
+            hdr[slot] = (c, op)
+            if op is not None and op[0]:
+                full[slot].arrive(tx=32768)
+                flight.append([slot, rng.choice([1, 3, 10, 80, 400])])
+            else:
+                full[slot].arrive()
+            slot += 1
+            if slot == NST:
+                slot, phase = 0, phase ^ 1
+            yield
+
+    def consumer(g):
+        slot, phase, cph, expect = g, 0, 0, g
+        while True:
+            if gate and ngroups > 1:
+                while not empty[slot].passed(phase ^ 1):
+                    yield
+            while not full[slot].passed(phase):
+                yield
+            c, op = hdr[slot]
+            if c != expect:
+                raise AssertionError(f"group {g} consumed stage {c}, expected {expect}")
+            expect += ngroups
+            if op is None:
+                return
+            for _ in range(rng.randint(0, 3)):
+                yield
+            empty[slot].arrive()
+            slot += ngroups
+            if slot >= NST:
+                slot, phase = slot - NST, phase ^ 1
+            if op[1]:
+                for _ in range(op[2]):
+                    for _ in range(32):
+                        csync.arrive()
+                    while not csync.passed(cph):
+                        yield
+                    cph ^= 1
+
+    actors = [producer()] + [consumer(g) for g in range(ngroups) for _ in range(WPG)]
+    alive, steps = list(actors), 0
+    while alive:
+        steps += 1
+        assert steps < 2_000_000, "deadlock"
+        for f in list(flight):
+            f[1] -= 1
+            if f[1] <= 0:
+                full[f[0]].complete_tx(32768)
+                flight.remove(f)
+        a = rng.choice(alive)
+        try:
+            next(a)
+        except StopIteration:
+            alive.remove(a)
+
+
+@pytest.mark.parametrize("ngroups", [1, 2])
+def test_ring_protocol(ngroups):
+    for seed in range(40):
+        rng = random.Random(seed)
+        pieces = [rng.choice([1, 2, 3, 4, 5, 7, 12, 40]) for _ in range(rng.randint(1, 10))]
+        simulate(pieces, ngroups, gate=True, seed=seed)
+
+
+def test_two_groups_without_gate_consume_stale_stage():
+    failures = 0
+    for seed in range(40):
+        rng = random.Random(seed)
+        pieces = [rng.choice([1, 2, 3, 4, 5, 7, 12, 40]) for _ in range(rng.randint(1, 10))]
+        try:
+            simulate(pieces, 2, gate=False, seed=seed)
+        except AssertionError:
+            failures += 1
+    assert failures > 0
