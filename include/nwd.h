@@ -126,6 +126,25 @@ int nwd_attn_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* 
                     uint32_t seq, uint32_t cap, float scale, void* workspace, size_t ws_bytes,
                     void* stream);
 
+/* Same computation as nwd_attn_decode, for callers that cannot allocate
+ * device memory: a host that only receives buffers it did not create (a
+ * JavaScript engine handing over existing GPU buffers through an addon, an
+ * embedder with a fixed memory budget) has no way to provide the workspace.
+ * This entry point takes none.  It allocates nothing; its scratch is a
+ * fixed array built into the library (about 1.3 MB, which every GPU that
+ * loads the library keeps until the process exits), sized for one sequence
+ * with up to 64 kv heads on up to 160 SMs; larger shapes return
+ * NWD_ERR_UNSUPPORTED.  The first call on a device looks up the scratch's
+ * device address; make that first call before any stream capture.  All calls
+ * share the one scratch: calls that may overlap on the GPU (different
+ * streams, or different host threads) race and must be serialised by the
+ * caller.  Each call clears the scratch's header on `stream` before its
+ * launch.  No counterpart in the reference. */
+int nwd_attn_decode_noalloc(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                            uint16_t* o, uint32_t n_heads, uint32_t n_kv_heads,
+                            uint32_t head_dim, uint32_t seq, uint32_t cap, float scale,
+                            void* stream);
+
 /* One engine attention step (engine/runtime.js:389-391 with the uniforms of
  * :451-452): writes k_new/v_new ([n_kv_heads, head_dim]) into row `seq` of the
  * caches, then attends over rows 0..seq (seq + 1 rows), in one launch. */

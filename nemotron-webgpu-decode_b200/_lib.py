@@ -56,6 +56,8 @@ SIGNATURES = {
     "nwd_workspace_check": (ctypes.c_int, [_P, _sz, ctypes.POINTER(_u32), _P]),
     "nwd_attn_decode": (ctypes.c_int, [_P, _P, _P, _P, _u32, _u32, _u32, _u32, _u32, _f32, _P,
                                        _sz, _P]),
+    "nwd_attn_decode_noalloc": (ctypes.c_int, [_P, _P, _P, _P, _u32, _u32, _u32, _u32, _u32,
+                                               _f32, _P]),
     "nwd_kv_append_attn_decode": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _u32, _u32, _u32, _u32,
                                                  _u32, _f32, _P, _sz, _P]),
     "nwd_attn_decode_batched": (ctypes.c_int, [_P, _P, _P, _u64, _P, _P, _P, _u32, _u32, _u32,

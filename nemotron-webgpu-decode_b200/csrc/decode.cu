@@ -39,6 +39,7 @@
 
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 
 #include "nwd_common.h"
 
@@ -1034,6 +1035,40 @@ int launch(const Call& c) {
   return ok();
 }
 
+// ---- scratch for nwd_attn_decode_noalloc ----
+// Callers that cannot allocate device memory get the decode's scratch (work
+// header, merge tickets, partial slots) from this file-scope array instead of
+// a caller workspace.  Its size covers one sequence with up to
+// NOALLOC_MAX_KV_HEADS kv heads, a GQA group up to GMAX and up to
+// NOALLOC_MAX_SMS SMs (two partial slots per SM).  Every GPU that loads the
+// library holds it until the process exits.
+constexpr uint32_t NOALLOC_MAX_KV_HEADS = 64;
+constexpr uint32_t NOALLOC_MAX_SMS = 160;
+constexpr size_t NOALLOC_BYTES =
+    256 /* header */ + 256 /* tickets: 64 kv heads x 4 B */ +
+    (size_t)2 * NOALLOC_MAX_SMS * GMAX * 2 * sizeof(float) /* (m, l) per slot and head */ +
+    (size_t)2 * NOALLOC_MAX_SMS * GMAX * HD * sizeof(float) /* o per slot and head */;
+__device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_BYTES];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+// Device address of the scratch on the current device.  Host code only sees
+// a host-side stand-in for a __device__ array, so the address is looked up
+// once per device (with that device current) and cached.
+int noalloc_scratch(int device, void** out) {
+  using namespace nwd;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[device]) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(decode scratch)");
+    g_noalloc_ptr[device] = ptr;
+  }
+  *out = g_noalloc_ptr[device];
+  return NWD_OK;
+}
+
 }  // namespace
 
 using namespace nwd;
@@ -1063,6 +1098,41 @@ int nwd_attn_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* 
   c.single_len = (int32_t)seq; c.o = o; c.batch = 1;
   c.n_heads = n_heads; c.n_kv = n_kv_heads; c.hd = head_dim; c.scale = scale;
   c.ws = workspace; c.ws_bytes = ws_bytes; c.stream = stream; c.who = "nwd_attn_decode";
+  return launch(c);
+}
+
+int nwd_attn_decode_noalloc(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                            uint16_t* o, uint32_t n_heads, uint32_t n_kv_heads,
+                            uint32_t head_dim, uint32_t seq, uint32_t cap, float scale,
+                            void* stream) {
+  const char* who = "nwd_attn_decode_noalloc";
+  if (seq > cap) return fail(NWD_ERR_RANGE, "seq %u exceeds maxSeq %u", seq, cap);
+  int st = check_shape(n_heads, n_kv_heads, head_dim, who);
+  if (st) return st;
+  if (n_kv_heads > NOALLOC_MAX_KV_HEADS)
+    return fail(NWD_ERR_UNSUPPORTED, "%s: n_kv_heads %u exceeds the built-in scratch limit of %u",
+                who, n_kv_heads, NOALLOC_MAX_KV_HEADS);
+  DeviceInfo di;
+  st = current_device_info(&di);
+  if (st) return st;
+  const WsLayout lay = ws_layout(1, n_kv_heads, n_heads / n_kv_heads, head_dim, slots_for(di));
+  if ((uint32_t)di.sm_count > NOALLOC_MAX_SMS || lay.total > NOALLOC_BYTES)
+    return fail(NWD_ERR_UNSUPPORTED,
+                "%s: needs %zu bytes of scratch on this device (%d SMs); the built-in scratch "
+                "holds %zu",
+                who, lay.total, di.sm_count, NOALLOC_BYTES);
+  void* scratch = nullptr;
+  st = noalloc_scratch(di.device, &scratch);
+  if (st) return st;
+  // The scratch keeps the previous call's contents: the header and merge
+  // tickets must start at zero, so clear them (no allocation involved).
+  cudaError_t e = cudaMemsetAsync(scratch, 0, lay.ml_off, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "clearing the decode scratch");
+  Call c{};
+  c.q = q; c.k_pool = k_cache; c.v_pool = v_cache; c.pool_rows = cap;
+  c.single_len = (int32_t)seq; c.o = o; c.batch = 1;
+  c.n_heads = n_heads; c.n_kv = n_kv_heads; c.hd = head_dim; c.scale = scale;
+  c.ws = scratch; c.ws_bytes = NOALLOC_BYTES; c.stream = stream; c.who = who;
   return launch(c);
 }
 
