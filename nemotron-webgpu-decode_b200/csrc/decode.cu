@@ -39,6 +39,7 @@
 
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
 #include <mutex>
 
 #include "nwd_common.h"
@@ -87,6 +88,7 @@ struct Params {
   uint32_t partial;  // write (m, l, o) partials instead of O
   uint32_t min_chunk;  // least rows (x kv heads) per CTA range
   uint32_t pair_max;   // one CTA per (sequence, kv head) when every pair is this short
+  uint32_t split_k;    // > 0: CTA i takes piece i % k of pair i / k (k equal pieces per pair)
 };
 
 // ---- shared memory layout (offsets from a 1024-aligned base) ----
@@ -380,7 +382,12 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
   // Work split.  Pair mode (small problems): CTA i takes the whole pair i, no
   // partials.  Otherwise every CTA takes an equal range [x0, x1) of the
   // flattened (pair, row) space, T = n_kv * all rows.
-  const bool pair_mode = (uint64_t)B * p.n_kv <= gridDim.x && misc->max_rows <= p.pair_max;
+  // Aligned split: CTA i takes piece i % k of pair i / k, the pair's rows cut
+  // into k equal pieces (k = 1: one CTA per pair, no partials).  Chosen by the
+  // host for a single sequence, or here for small problems.
+  uint32_t split_k = p.split_k;
+  if (split_k == 0 && (uint64_t)B * p.n_kv <= gridDim.x && misc->max_rows <= p.pair_max)
+    split_k = 1;
   const uint64_t T = (uint64_t)p.n_kv * total32;
   uint64_t W = udiv64(T + gridDim.x - 1, gridDim.x);
   if (W < p.min_chunk) W = p.min_chunk;
@@ -483,12 +490,16 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
       }
     };
 
-    if (pair_mode) {
-      const uint32_t i = blockIdx.x;
-      if (i < B * p.n_kv) {
-        const uint32_t b = i / p.n_kv, hkv = i % p.n_kv;
+    if (split_k) {
+      const uint32_t pair = blockIdx.x / split_k, j = blockIdx.x % split_k;
+      if (pair < B * p.n_kv) {
+        const uint32_t b = pair / p.n_kv, hkv = pair % p.n_kv;
         const uint32_t L = S[b + 1] - S[b];
-        if (L > 0) emit_piece(b, hkv, L, 0, L, true, (int32_t)i, (int32_t)i);
+        const uint32_t t0 = (uint32_t)((uint64_t)j * L / split_k);
+        const uint32_t t1 = (uint32_t)((uint64_t)(j + 1) * L / split_k);
+        if (t1 > t0)
+          emit_piece(b, hkv, L, t0, t1, split_k == 1, (int32_t)(pair * split_k),
+                     (int32_t)(pair * split_k + split_k - 1));
       }
     } else if (x0 < x1) {
       // locate the first piece, then walk pairs forward (no further division
@@ -1002,10 +1013,21 @@ int launch(const Call& c) {
   // kv head when the sequence is short, else only as many CTAs as ranges of
   // min_chunk items
   uint32_t grid = grid_max;
+  p.split_k = 0;
   if (!c.seq_len) {
+    // single sequence: cut each kv head's rows into k equal pieces, one CTA
+    // each (k = 1 for short sequences: no partials), so no CTA straddles two
+    // heads; fall back to the flattened split when there are more kv heads
+    // than SMs
     const uint64_t rows = (uint64_t)(c.single_len > 0 ? c.single_len : 0);
-    if (c.n_kv <= grid_max && rows <= tu.pair_max) {
-      grid = c.n_kv;
+    if (c.n_kv <= grid_max) {
+      uint64_t k = 1;
+      if (rows > tu.pair_max) {
+        k = std::min<uint64_t>(grid_max / c.n_kv, (rows + tu.min_chunk - 1) / tu.min_chunk);
+        if (k < 1) k = 1;
+      }
+      p.split_k = (uint32_t)k;
+      grid = c.n_kv * (uint32_t)k;
     } else {
       const uint64_t need = (c.n_kv * rows + tu.min_chunk - 1) / tu.min_chunk;
       if (need < grid) grid = (uint32_t)need;

@@ -27,22 +27,31 @@ TOK, NST, WPG = 64, 5, 4
 
 # ---------------------------------------------------------------- planner
 
-def plan(lens, nkv, grid, min_chunk=256, pair_max=512):
-    """Pieces (cta, b, hkv, t0, t1, complete, f, l) as decode_kernel walks them."""
+def plan(lens, nkv, grid, min_chunk=256, pair_max=512, split_k=0):
+    """Pieces (cta, b, hkv, t0, t1, complete, f, l) as decode_kernel walks them.
+
+    split_k > 0: CTA i takes piece i % k of pair i / k (the host's choice for a
+    single sequence); otherwise one CTA per pair for small problems, else the
+    flattened equal-range split."""
     B = len(lens)
     S = [0]
     for L in lens:
         S.append(S[-1] + L)
     T = nkv * S[B]
-    pair_mode = B * nkv <= grid and max(lens) <= pair_max
+    if split_k == 0 and B * nkv <= grid and max(lens) <= pair_max:
+        split_k = 1
     W = max((T + grid - 1) // grid, min_chunk)
     out = []
     for i in range(grid):
-        if pair_mode:
-            if i < B * nkv:
-                b, h = divmod(i, nkv)
-                if lens[b]:
-                    out.append((i, b, h, 0, lens[b], True, i, i))
+        if split_k:
+            pair, j = divmod(i, split_k)
+            if pair < B * nkv:
+                b, h = divmod(pair, nkv)
+                L = lens[b]
+                t0, t1 = j * L // split_k, (j + 1) * L // split_k
+                if t1 > t0:
+                    out.append((i, b, h, t0, t1, split_k == 1, pair * split_k,
+                                pair * split_k + split_k - 1))
             continue
         x0, x1 = min(T, i * W), min(T, i * W + W)
         if x0 >= x1:
@@ -96,6 +105,22 @@ def check_plan(lens, nkv, grid, **kw):
                 assert l - f + 1 == len(ps)
                 assert [p[2] for p in ps] == list(range(f, l + 1))
     return pieces
+
+
+def host_split(L, nkv, sms=148, min_chunk=256, pair_max=512):
+    """The host's choice for a single sequence: (grid, k)."""
+    k = 1 if L <= pair_max else max(1, min(sms // nkv, -(-L // min_chunk)))
+    return nkv * k, k
+
+
+def test_planner_single_sequence_aligned_split():
+    for L in (1, 151, 512, 513, 1024, 4097, 32768, 262144, 1 << 20):
+        for nkv in (1, 8, 16):
+            grid, k = host_split(L, nkv)
+            pieces = check_plan([L], nkv, grid, split_k=k)
+            # every CTA holds at most one piece: no CTA straddles two kv heads
+            ctas = [p[0] for p in pieces]
+            assert len(ctas) == len(set(ctas))
 
 
 def test_planner_bench_shapes():
