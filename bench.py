@@ -165,6 +165,15 @@ def seeds_for(rank):
             "kn": 3003 + 100 * rank, "vn": 3004 + 100 * rank}
 
 
+def max_over_ranks(values, dist=None, device=None):
+    """Element-wise max of per-rank floats (timings) across ranks (no-op at N=1)."""
+    import torch
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
+    if dist is not None and dist.is_initialized() and dist.get_world_size() > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t.tolist()]
+
+
 def step_bytes(L_attended):
     """Algorithmic HBM bytes of one step: K+V rows read, q read + o write, new K/V row read+write."""
     B = len(L_attended)
@@ -306,7 +315,7 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=30)
     ap.add_argument("--impl", choices=["nwd", "reference"], default="nwd")
-    ap.add_argument("--config", choices=["3", "1", "2"], default="3")
+    ap.add_argument("--config", choices=["3", "1", "2", "5"], default="3")
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
     ap.add_argument("--ramp-seconds", type=float, default=1.0)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -337,6 +346,8 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     ops = import_pkg()
+    if args.config == "5":
+        return run_config5(args, ops, torch, dist, dev, rank, world)
     if args.config != "3":
         return run_small_configs(args, ops, torch, dev, rank, world)
 
@@ -440,10 +451,7 @@ def main():
         return 3
 
     # max over ranks
-    vals_t = torch.tensor([ms, e2e["ms"] if e2e else 0.0], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(vals_t, op=dist.ReduceOp.MAX)
-    ms_max, e2e_ms_max = float(vals_t[0]), float(vals_t[1])
+    ms_max, e2e_ms_max = max_over_ranks([ms, e2e["ms"] if e2e else 0.0], dist, dev)
     if sampler:
         sampler.stop()
     if rank == 0:
@@ -569,6 +577,109 @@ def run_small_configs(args, ops, torch, dev, rank, world):
     for ln in out:
         print(json.dumps(ln), flush=True)
     return 0
+
+
+def run_config5(args, ops, torch, dist, dev, rank, world):
+    """4 sequences x 1 048 576 rows (Hq=32, Hkv=8), each sequence's
+    rows sharded contiguously over the ranks; a step is the shard partial on every
+    GPU, one NCCL all-gather of the partials and the LSE merge (mgpu.ShardedDecode).
+    The K/V data is the same stream whatever the rank count (fill offsets follow
+    the global row index), so every N computes the same O."""
+    mgpu = importlib.import_module(PKG + ".mgpu")
+    B, L = 4, 1 << 20
+    if args.kv_len:
+        L = args.kv_len
+    sd = mgpu.ShardedDecode([L] * B, HQ, HKV, HD, device=dev)
+    row_elems = HKV * HD
+    for b in range(B):
+        lo, hi = sd.global_rows(b)
+        off = int(sd.row_offset[b])
+        n = hi - lo
+        ops.fill_normal(sd.k_pool[off:off + n], 5000, (b * L + lo) * row_elems)
+        ops.fill_normal(sd.v_pool[off:off + n], 5001, (b * L + lo) * row_elems)
+    q = ops.fill_normal(torch.empty(B, HQ, HD, dtype=torch.float16, device=dev), 5002)
+    o = torch.empty(B, HQ, HD, dtype=torch.float16, device=dev)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        sd.step(q, o)
+    barrier()
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        sd.step(q, o)
+    e.record()
+    e.synchronize()
+    barrier()
+    ms = a.elapsed_time(e)
+    # roofline of the shard kernel alone (per-launch events, same stream)
+    R = min(args.steps, 20)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(R)]
+    for i in range(R):
+        evs[i][0].record()
+        sd.partial_fn(q)
+        evs[i][1].record()
+    torch.cuda.synchronize()
+    kern_ms = statistics.mean(x.elapsed_time(y) for x, y in evs)
+    local_rows = sum(hi - lo for lo, hi in (sd.global_rows(b) for b in range(B)))
+    kern_bytes = 4096.0 * local_rows + B * HQ * HD * 2 + B * HQ * (HD + 2) * 4
+    # e2e: q from pinned host memory, O back to host, every step
+    q_h = q.cpu().pin_memory()
+    o_h = torch.empty(B, HQ, HD, dtype=torch.float16, pin_memory=True)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        q.copy_(q_h, non_blocking=True)
+        sd.step(q, o)
+        o_h.copy_(o, non_blocking=True)
+        stream.synchronize()
+    barrier()
+    a2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a2.record()
+    for _ in range(args.steps):
+        q.copy_(q_h, non_blocking=True)
+        sd.step(q, o)
+        o_h.copy_(o, non_blocking=True)
+        stream.synchronize()
+    e2.record()
+    e2.synchronize()
+    barrier()
+    e2e_ms = a2.elapsed_time(e2)
+    ms_max, e2e_max = max_over_ranks([ms, e2e_ms], dist, dev)
+    err = sd.workspace.check()
+    if rank == 0:
+        peak, kind = peaks()
+        total_bytes = 4096.0 * B * L + B * HQ * HD * 4
+        line = {
+            "metric": METRIC, "value": B * args.steps / (ms_max * 1e-3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "hbm_tbs": total_bytes / (ms_max * 1e-3 / args.steps) / 1e12,
+            "config": {"workload": "config5-long-context-split-kv", "sequences": B,
+                       "kv_len": L, "heads": HQ, "kv_heads": HKV, "head_dim": HD,
+                       "parallelism": f"rows sharded x{world}, NCCL all-gather of partials",
+                       "step": "shard partial + all-gather + LSE merge"},
+            "roofline": {"bound": "hbm", "achieved": kern_bytes / (kern_ms * 1e-3) / 1e9,
+                         "peak": peak, "unit": "GB/s",
+                         "frac": kern_bytes / (kern_ms * 1e-3) / 1e9 / peak,
+                         "kernel": "decode_kernel (partial mode), per rank",
+                         "launch_ms": kern_ms, "peak_source": kind},
+            "e2e": {"value": B * args.steps / (e2e_max * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": B * HQ * HD * 2, "d2h_bytes_per_step": B * HQ * HD * 2},
+            "gpu_launches": 2 * args.steps,
+            "device_error": err,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0 if err == 0 else 3
 
 
 if __name__ == "__main__":

@@ -248,3 +248,21 @@ def test_long_sequence_262k(ops, oracle):
                   ops.AttnParams(nh, nkv, hd, L))
     ref = oracle.attention_batched(q, k, v, [0], [L], nh, nkv, hd, f64=True)[0]
     assert_attn_close(vals(o), ref, "L=262144")
+
+
+def test_long_context_1m_rows_via_sharded_path(oracle):
+    """A 1 048 576-row sequence (Hq=8, Hkv=2: 1 GiB of K+V) through the shard
+    partial + merge path of mgpu.ShardedDecode (one process holds the shard)."""
+    import importlib
+    mgpu = importlib.import_module("nemotron-webgpu-decode_b200.mgpu")
+    nh, nkv, hd, L = 8, 2, 128, 1 << 20
+    sd = mgpu.ShardedDecode([L], nh, nkv, hd, device="cuda")
+    k = oracle.normal_f16(L * nkv * hd, 61)
+    v = oracle.normal_f16(L * nkv * hd, 62)
+    q = oracle.normal_f16(nh * hd, 63)
+    sd.k_pool.copy_(to_dev(k, (L, nkv, hd)))
+    sd.v_pool.copy_(to_dev(v, (L, nkv, hd)))
+    out = sd.step(to_dev(q, (1, nh, hd)))
+    ref = oracle.attention_batched(q, k, v, [0], [L], nh, nkv, hd, f64=True)
+    assert_attn_close(vals(out), ref, "L=1M sharded path")
+    assert sd.workspace.check() == 0
