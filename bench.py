@@ -143,6 +143,12 @@ def import_oracle():
         sys.path.insert(0, p)
     import oracle
     oracle.build()
+    # all host cores this process may run on (torchrun sets OMP_NUM_THREADS=1)
+    try:
+        cores = len(os.sched_getaffinity(0))
+    except AttributeError:
+        cores = os.cpu_count() or 1
+    oracle.set_num_threads(cores)
     return oracle
 
 
