@@ -200,6 +200,39 @@ int nwd_attn_merge(const float* part_o, const float* part_ml, uint16_t* o, uint3
                    uint32_t batch, uint32_t n_heads, uint32_t head_dim, void* stream);
 
 /* ------------------------------------------------------------------ */
+/* Prompt chunks (causal prefill)                                      */
+/* ------------------------------------------------------------------ */
+
+/* The kv_append path for a prompt chunk: kernels/kv_append.wgsl:13-18 for
+ * n_rows consecutive rows per sequence.  Sequence b's rows
+ * [b, 0..n_rows) of k_src / v_src ([batch, n_rows, n_kv, hd]) go to pool rows
+ * row_offset[b] + start_pos + i.  Rows outside the pool are skipped and
+ * flagged (NWD_DEVERR_ROW_RANGE) in the workspace's error word when a
+ * workspace is given (may be NULL).  Bit-exact. */
+int nwd_kv_append_rows(const uint16_t* k_src, const uint16_t* v_src, uint16_t* k_pool,
+                       uint16_t* v_pool, uint64_t pool_rows, const int64_t* row_offset,
+                       uint32_t start_pos, uint32_t n_rows, uint32_t batch, uint32_t n_kv,
+                       uint32_t hd, void* workspace, size_t ws_bytes, void* stream);
+
+/* Causal attention for a prompt chunk of n_q tokens per sequence on the
+ * tcgen05 tensor cores (TMEM accumulators).  The reference feeds a prompt one
+ * decode step per token (engine/runtime.js:640-643), so token i of a chunk
+ * whose K/V rows sit at start_pos .. start_pos+n_q-1 attends rows
+ * 0 .. start_pos+i: kernels/sparse_attn.wgsl once per token, computed here as
+ * one dense contraction.
+ *   q, o          : [batch, n_q, n_heads, head_dim]
+ *   k_pool, v_pool: [pool_rows, n_kv_heads, head_dim]; sequence b's rows start
+ *                   at pool row row_offset[b] (device int64[batch]) and must
+ *                   already hold the chunk's rows (nwd_kv_append_rows)
+ * head_dim 128; any GQA group.  workspace: >= 256 bytes, zeroed, 256-byte
+ * aligned (a decode workspace serves); its first word receives device errors. */
+int nwd_attn_prefill(const uint16_t* q, const uint16_t* k_pool, const uint16_t* v_pool,
+                     uint64_t pool_rows, const int64_t* row_offset, uint16_t* o, uint32_t batch,
+                     uint32_t n_q, uint32_t start_pos, uint32_t n_heads, uint32_t n_kv_heads,
+                     uint32_t head_dim, float scale, void* workspace, size_t ws_bytes,
+                     void* stream);
+
+/* ------------------------------------------------------------------ */
 /* Synthetic inputs                                                    */
 /* ------------------------------------------------------------------ */
 

@@ -24,7 +24,7 @@ cudaError_t g_encode_err = cudaSuccess;
 struct TmapEntry {
   const void* base;
   uint64_t rows;
-  uint32_t n_kv, hd, box_rows;
+  uint32_t n_kv, hd, box_rows, box_chunks;
   int device;
   CUtensorMap map;
 };
@@ -76,13 +76,14 @@ int current_device_info(DeviceInfo* out) {
 }
 
 int kv_tensor_map(CUtensorMap* out, const void* base, uint64_t rows, uint32_t n_kv, uint32_t hd,
-                  uint32_t box_rows) {
+                  uint32_t box_rows, uint32_t box_chunks) {
   int dev = 0;
   cudaGetDevice(&dev);
+  if (box_chunks == 0) box_chunks = hd / 64;
   for (int i = 0; i < kTmapCache; i++) {
     TmapEntry& t = g_tmaps[i];
     if (t.base == base && t.rows == rows && t.n_kv == n_kv && t.hd == hd &&
-        t.box_rows == box_rows && t.device == dev) {
+        t.box_rows == box_rows && t.box_chunks == box_chunks && t.device == dev) {
       *out = t.map;
       return NWD_OK;
     }
@@ -104,7 +105,7 @@ int kv_tensor_map(CUtensorMap* out, const void* base, uint64_t rows, uint32_t n_
     return fail(NWD_ERR_INVALID, "cache rows %llu outside [1, 2^31]", (unsigned long long)rows);
   cuuint64_t dims[4] = {64, hd / 64, n_kv, rows};
   cuuint64_t strides[3] = {128, (cuuint64_t)hd * 2, (cuuint64_t)n_kv * hd * 2};
-  cuuint32_t box[4] = {64, hd / 64, 1, box_rows};
+  cuuint32_t box[4] = {64, box_chunks, 1, box_rows};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUtensorMap map;
   CUresult r = g_encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims,
@@ -123,6 +124,7 @@ int kv_tensor_map(CUtensorMap* out, const void* base, uint64_t rows, uint32_t n_
   t.n_kv = n_kv;
   t.hd = hd;
   t.box_rows = box_rows;
+  t.box_chunks = box_chunks;
   t.device = dev;
   t.map = map;
   *out = map;

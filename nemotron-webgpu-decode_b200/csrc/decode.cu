@@ -43,8 +43,11 @@
 #include <mutex>
 
 #include "nwd_common.h"
+#include "ptx.cuh"
 
 namespace {
+
+using namespace nwd::ptx;
 
 using nwd::WsHeader;
 
@@ -126,86 +129,6 @@ struct Misc {
 static_assert(sizeof(Misc) <= 64, "misc block");
 
 constexpr float RESCALE_LOG2 = 8.f;  // lazy-rescale threshold (log2 units)
-constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s
-constexpr uint32_t WAIT_LIMIT_ITERS = 1u << 26;
-
-// ---------------- PTX wrappers ----------------
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ uint64_t globaltimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait.  Returns false if the CTA is aborting (another thread gave
-// up) or this wait ran past its limits (then it raises the abort itself).
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int32_t* abort,
-                                          uint32_t* dev_err) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  for (uint32_t i = 1;; i++) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 31) == 0) {
-      if (*abort) return false;
-      if (i >= WAIT_LIMIT_ITERS || globaltimer() - t0 > WAIT_LIMIT_NS) {
-        *abort = 1;
-        atomicOr(dev_err, NWD_DEVERR_PIPE_TIMEOUT);
-        return false;
-      }
-    }
-  }
-}
-// Warp-uniform bounded wait: every lane waits (so every lane acquires the
-// barrier's completion), then the warp agrees; if any lane gave up, all do.
-__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int32_t* abort,
-                                          uint32_t* dev_err) {
-  const bool ok = mbar_wait(bar, parity, abort, dev_err);
-  return __all_sync(0xffffffffu, ok);
-}
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                            int c0, int c1, int c2, int c3, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
-      "l"(policy)
-      : "memory");
-}
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
-                                          uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          dst),
-      "l"(src), "r"(bytes), "r"(bar)
-      : "memory");
-}
-__device__ __forceinline__ uint64_t evict_first_policy() {
-  uint64_t p;
-  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
                                         uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"

@@ -27,9 +27,11 @@ int current_device_info(DeviceInfo* out);
 // ---- TMA descriptors ----
 // Encodes (or returns a cached copy of) the 4-D tensor map the decode kernel
 // uses for a token-major cache [rows, n_kv, hd] of fp16:
-//   dims {64, hd/64, n_kv, rows}, box {64, hd/64, 1, box_rows}, 128-byte swizzle.
+//   dims {64, hd/64, n_kv, rows}, box {64, box_chunks, 1, box_rows}, 128-byte
+//   swizzle (box_chunks = hd/64 loads whole rows; 1 loads one 64-wide column
+//   chunk, the layout the tcgen05 operand descriptors expect).
 int kv_tensor_map(CUtensorMap* out, const void* base, uint64_t rows, uint32_t n_kv, uint32_t hd,
-                  uint32_t box_rows);
+                  uint32_t box_rows, uint32_t box_chunks = 0);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

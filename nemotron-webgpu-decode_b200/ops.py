@@ -237,6 +237,60 @@ def merge(part_o, part_ml, o, stream=None) -> torch.Tensor:
     return o
 
 
+class Scratch:
+    """A zeroed 256-byte-aligned device header for calls that only need the
+    error word (prefill, multi-row appends)."""
+
+    def __init__(self, device=None):
+        device = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        self._buf = torch.zeros(512, dtype=torch.uint8, device=device)
+        self.ptr = (self._buf.data_ptr() + 255) // 256 * 256
+        self.nbytes = 256
+
+    def check(self, stream=None) -> int:
+        v = ctypes.c_uint32(0)
+        call("nwd_workspace_check", self.ptr, self.nbytes, ctypes.byref(v), _stream(stream))
+        return int(v.value)
+
+
+_scratch_cache: dict = {}
+
+
+def _scratch(device, ws):
+    if ws is not None:
+        return ws
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    if key not in _scratch_cache:
+        _scratch_cache[key] = Scratch(device)
+    return _scratch_cache[key]
+
+
+def kv_append_rows(k_src, v_src, k_pool, v_pool, row_offset, start_pos: int, workspace=None,
+                   stream=None) -> None:
+    """Prompt-chunk rows [batch, n_rows, n_kv, hd] into pool rows row_offset[b] + start_pos + i."""
+    batch, n_rows, n_kv, hd = k_src.shape
+    rows = k_pool.numel() // (n_kv * hd)
+    ws = _scratch(k_src.device, workspace)
+    call("nwd_kv_append_rows", _h(k_src, "k_src"), _h(v_src, "v_src"), _h(k_pool, "k_pool"),
+         _h(v_pool, "v_pool"), rows, _ptr(row_offset, torch.int64, "row_offset"), start_pos,
+         n_rows, batch, n_kv, hd, ws.ptr, ws.nbytes, _stream(stream))
+
+
+def attention_prefill(q, k_pool, v_pool, row_offset, o, start_pos: int, n_heads: int,
+                      n_kv_heads: int, head_dim: int = 128, scale: float = 0.0, workspace=None,
+                      stream=None) -> torch.Tensor:
+    """Causal prefill of a chunk: q/o [batch, n_q, n_heads, hd]; token i attends pool rows
+    row_offset[b] + [0, start_pos + i] (tcgen05 tensor cores)."""
+    batch, n_q = q.shape[0], q.shape[1]
+    rows = k_pool.numel() // (n_kv_heads * head_dim)
+    ws = _scratch(q.device, workspace)
+    call("nwd_attn_prefill", _h(q, "q"), _h(k_pool, "k_pool"), _h(v_pool, "v_pool"), rows,
+         _ptr(row_offset, torch.int64, "row_offset"), _h(o, "o"), batch, n_q, start_pos, n_heads,
+         n_kv_heads, head_dim, float(scale), ws.ptr, ws.nbytes, _stream(stream))
+    return o
+
+
 def fill_normal(t: torch.Tensor, seed: int, offset: int = 0, stream=None) -> torch.Tensor:
     """Fill an fp16 tensor with the deterministic N(0,1) stream (bit-identical to the CPU
     generator used by the tests)."""
@@ -247,5 +301,6 @@ def fill_normal(t: torch.Tensor, seed: int, offset: int = 0, stream=None) -> tor
 __all__ = [
     "KvParams", "AttnParams", "Workspace", "NwdError", "kv_append", "kv_append_kv",
     "kv_append_batched", "attention", "kv_append_attention", "attention_batched",
-    "kv_append_attention_batched", "attention_partial", "merge", "fill_normal",
+    "kv_append_attention_batched", "attention_partial", "merge", "fill_normal", "Scratch",
+    "kv_append_rows", "attention_prefill",
 ]

@@ -239,6 +239,38 @@ void oracle_attn_f32(const uint16_t* q, const uint16_t* k_cache, const uint16_t*
     oracle_attn_batched_f32(q, k_cache, v_cache, &off, &L, out, 1, n_heads, n_kv, hd, scale);
 }
 
+/* ---------------- causal prefill ---------------- */
+
+/* The reference has no prefill: it runs the prompt one decode step per token
+ * (engine/runtime.js:640-643), so token i of a chunk starting at row
+ * start_pos attends rows 0 .. start_pos + i.  This is exactly that: one
+ * kernels/sparse_attn.wgsl evaluation per (sequence, token, head).
+ *   q, out: [batch, n_q, n_heads, hd]; pools [rows, n_kv, hd];
+ *   sequence b's rows start at pool row row_offset[b]. */
+void oracle_attn_prefill_f32(const uint16_t* q, const uint16_t* k_pool, const uint16_t* v_pool,
+                             const int64_t* row_offset, float* out, uint32_t batch, uint32_t n_q,
+                             uint32_t start_pos, uint32_t n_heads, uint32_t n_kv, uint32_t hd,
+                             float scale) {
+    scale = default_scale(hd, scale);
+    uint32_t group = n_heads / n_kv;
+    int64_t total = (int64_t)batch * n_q * n_heads;
+#pragma omp parallel
+    {
+        float* scores = (float*)malloc(sizeof(float) * (start_pos + n_q + 1));
+#pragma omp for schedule(dynamic, 16)
+        for (int64_t idx = 0; idx < total; idx++) {
+            uint32_t h = (uint32_t)(idx % n_heads);
+            uint32_t i = (uint32_t)((idx / n_heads) % n_q);
+            uint32_t b = (uint32_t)(idx / ((int64_t)n_heads * n_q));
+            const uint64_t row0 = (uint64_t)row_offset[b] * n_kv * hd;
+            attn_head_f32(q + (uint64_t)idx * hd, k_pool + row0, v_pool + row0,
+                          out + (uint64_t)idx * hd, n_kv, h / group, hd, start_pos + i + 1, scale,
+                          scores);
+        }
+        free(scores);
+    }
+}
+
 /* ---------------- attention, f64 (drift check at long L) ---------------- */
 
 void oracle_attn_batched_f64(const uint16_t* q, const uint16_t* k_pool, const uint16_t* v_pool,

@@ -62,6 +62,8 @@ def lib():
         L.oracle_attn_partial.argtypes = [_u16p, _u16p, _u16p, _i64p, _i32p, _f32p, _f32p,
                                           _u32, _u32, _u32, _u32, ctypes.c_float]
         L.oracle_attn_merge.argtypes = [_f32p, _f32p, _f32p, _u32, _u32, _u32]
+        L.oracle_attn_prefill_f32.argtypes = [_u16p, _u16p, _u16p, _i64p, _f32p, _u32, _u32, _u32,
+                                              _u32, _u32, _u32, ctypes.c_float]
         L.oracle_num_threads.restype = ctypes.c_int
         L.oracle_set_num_threads.argtypes = [ctypes.c_int]
         _lib = L
@@ -160,6 +162,19 @@ def merge(part_o: np.ndarray, part_ml: np.ndarray) -> np.ndarray:
     out = np.empty((rows, hd), np.float32)
     lib().oracle_attn_merge(part_o.reshape(-1), part_ml.reshape(-1), out.reshape(-1), shards,
                             rows, hd)
+    return out
+
+
+def attention_prefill(q, k_pool, v_pool, row_offset, n_q: int, start_pos: int, n_heads: int,
+                      n_kv_heads: int, head_dim: int, scale: float = 0.0) -> np.ndarray:
+    """Causal prefill as the reference computes it (one decode step per prompt token):
+    q [batch, n_q, n_heads, hd] -> f32 [batch, n_q, n_heads, hd]."""
+    row_offset = np.ascontiguousarray(row_offset, dtype=np.int64)
+    batch = len(row_offset)
+    out = np.empty((batch, n_q, n_heads, head_dim), np.float32)
+    lib().oracle_attn_prefill_f32(_u16(q).reshape(-1), _u16(k_pool).reshape(-1),
+                                  _u16(v_pool).reshape(-1), row_offset, out.reshape(-1), batch,
+                                  n_q, start_pos, n_heads, n_kv_heads, head_dim, float(scale))
     return out
 
 
