@@ -52,6 +52,15 @@ def peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def tensor_peak():
+    """Dense bf16/fp16 TFLOP/s: the burst figure (a kernel timed alone)."""
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 def profiled_traffic(name: str):
     """dram bytes per launch from a committed ncu summary (profiles/<name>.txt), if any."""
     path = os.path.join(REPO, "profiles", name + ".txt")
@@ -321,7 +330,7 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=30)
     ap.add_argument("--impl", choices=["nwd", "reference"], default="nwd")
-    ap.add_argument("--config", choices=["3", "1", "2", "5"], default="3")
+    ap.add_argument("--config", choices=["3", "1", "2", "4", "5"], default="3")
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
     ap.add_argument("--ramp-seconds", type=float, default=1.0)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -354,6 +363,8 @@ def main():
     ops = import_pkg()
     if args.config == "5":
         return run_config5(args, ops, torch, dist, dev, rank, world)
+    if args.config == "4":
+        return run_config4(args, ops, torch, dist, dev, rank, world)
     if args.config != "3":
         return run_small_configs(args, ops, torch, dev, rank, world)
 
@@ -583,6 +594,116 @@ def run_small_configs(args, ops, torch, dev, rank, world):
     for ln in out:
         print(json.dumps(ln), flush=True)
     return 0
+
+
+def run_config4(args, ops, torch, dist, dev, rank, world):
+    """chunked causal prefill, 8 sequences x 2048 prompt tokens per GPU
+    (Hq=32, Hkv=8, d=128, scale 1/sqrt(128)).  A step writes the chunk's K/V rows through
+    the kv_append path (nwd_kv_append_rows) and runs the tcgen05 prefill attention.
+    Sequences shard across GPUs with no communication (weak scaling)."""
+    B, S = 8, 2048
+    rows = B * S
+    seed = 4000 + 100 * rank
+    f16 = torch.float16
+    k_pool = torch.empty(rows, HKV, HD, dtype=f16, device=dev)
+    v_pool = torch.empty_like(k_pool)
+    k_new = ops.fill_normal(torch.empty(B, S, HKV, HD, dtype=f16, device=dev), seed)
+    v_new = ops.fill_normal(torch.empty(B, S, HKV, HD, dtype=f16, device=dev), seed + 1)
+    q = ops.fill_normal(torch.empty(B, S, HQ, HD, dtype=f16, device=dev), seed + 2)
+    o = torch.empty(B, S, HQ, HD, dtype=f16, device=dev)
+    ro = torch.arange(B, dtype=torch.int64, device=dev) * S
+    ws = ops.Scratch(dev)
+    flops = 4.0 * B * HQ * HD * S * (S + 1) / 2  # causal: visible (query, key) pairs only
+
+    def step(qq=None, kk=None, vv=None, oo=None):
+        ops.kv_append_rows(k_new if kk is None else kk, v_new if vv is None else vv, k_pool,
+                           v_pool, ro, 0, workspace=ws)
+        ops.attention_prefill(q if qq is None else qq, k_pool, v_pool, ro,
+                              o if oo is None else oo, 0, HQ, HKV, HD, workspace=ws)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        step()
+    e.record()
+    e.synchronize()
+    barrier()
+    ms = a.elapsed_time(e)
+    # the prefill kernel alone, per-launch events
+    R = min(args.steps, 20)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(R)]
+    for i in range(R):
+        ops.kv_append_rows(k_new, v_new, k_pool, v_pool, ro, 0, workspace=ws)
+        evs[i][0].record()
+        ops.attention_prefill(q, k_pool, v_pool, ro, o, 0, HQ, HKV, HD, workspace=ws)
+        evs[i][1].record()
+    torch.cuda.synchronize()
+    kern_ms = statistics.mean(x.elapsed_time(y) for x, y in evs)
+    # e2e: the chunk's q, k, v from pinned host memory, o back, every step
+    q_h, k_h, v_h = q.cpu().pin_memory(), k_new.cpu().pin_memory(), v_new.cpu().pin_memory()
+    o_h = torch.empty_like(o, device="cpu").pin_memory()
+    qd, kd, vd, od = torch.empty_like(q), torch.empty_like(k_new), torch.empty_like(v_new), \
+        torch.empty_like(o)
+    stream = torch.cuda.current_stream()
+
+    def e2e_step():
+        qd.copy_(q_h, non_blocking=True)
+        kd.copy_(k_h, non_blocking=True)
+        vd.copy_(v_h, non_blocking=True)
+        step(qd, kd, vd, od)
+        o_h.copy_(od, non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    a2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a2.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e2.record()
+    e2.synchronize()
+    barrier()
+    ms_max, e2e_max = max_over_ranks([ms, a2.elapsed_time(e2)], dist, dev)
+    err = ws.check()
+    if rank == 0:
+        peak, kind = tensor_peak()
+        tflops = flops / (kern_ms * 1e-3) / 1e12
+        tokens = B * S * world * args.steps
+        line = {
+            "metric": METRIC, "value": tokens / (ms_max * 1e-3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "tflops": flops * world / (ms_max * 1e-3 / args.steps) / 1e12,
+            "config": {"workload": "config4-chunked-causal-prefill", "sequences_per_gpu": B,
+                       "chunk": S, "heads": HQ, "kv_heads": HKV, "head_dim": HD,
+                       "accumulate": "f32 (TMEM)",
+                       "step": "kv_append of the chunk's K/V rows + tcgen05 causal prefill",
+                       "flops_per_step_per_gpu": flops},
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
+                         "frac": tflops / peak, "kernel": "prefill_kernel",
+                         "launch_ms": kern_ms, "peak_source": f"{kind} (bf16_tflops, burst)"},
+            "e2e": {"value": tokens / (e2e_max * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": (q.numel() + 2 * k_new.numel()) * 2 * world,
+                    "d2h_bytes_per_step": o.numel() * 2 * world},
+            "gpu_launches": 2 * args.steps,
+            "device_error": err,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0 if err == 0 else 3
 
 
 def run_config5(args, ops, torch, dist, dev, rank, world):
