@@ -8,23 +8,30 @@
 //
 // One CTA per (sequence, query head, 128-query tile), 8 warps:
 //   warp 0      TMA producer: the Q tile once, then K and V tiles of 128 rows
-//               into a 2-stage ring (each 128-row tile as two 64-column
-//               chunks, 128-byte swizzle: the canonical K-major layout of the
-//               tcgen05 shared-memory descriptors).
-//   warp 1      MMA issuer (one thread): S = Q K^T into TMEM columns [0,128)
-//               (M=128 queries, N=128 keys, K=128 = 8 MMAs of K=16), then,
-//               once P is in shared memory, O += P V into TMEM columns
-//               [128,256) (V as an MN-major operand), P as an fp16 head and an
-//               fp16 remainder (16 MMAs): one fp16 rounding of P would exceed
-//               the parity tolerance on outputs near zero.  tcgen05.commit
-//               signals S ready, and PV done (which also frees the K/V stage).
-//   warp 2      TMEM allocation (256 columns) and release.
+//               into 2-stage rings with separate barriers (K(j) is free once
+//               S(j) is done, long before V(j)); each 128-row tile as two
+//               64-column chunks, 128-byte swizzle: the canonical K-major
+//               layout of the tcgen05 shared-memory descriptors.
+//   warp 1      MMA issuer (one thread): S(j) = Q K(j)^T into TMEM score
+//               buffer j & 1 (M=128 queries, N=128 keys, K=128 = 8 MMAs of
+//               K=16), issued one block ahead so it overlaps the softmax of
+//               block j-1; then, once P(j) is in TMEM, O += P V into TMEM
+//               columns [256,384) with A = P read from tensor memory and
+//               B = V an MN-major shared-memory operand.  P is an fp16 head
+//               and an fp16 remainder (16 MMAs): one fp16 rounding of P would
+//               exceed the parity tolerance on outputs near zero.
+//               tcgen05.commit signals S ready, K free, V free and PV done.
+//   warp 2      TMEM allocation (512 columns) and release.
 //   warps 4-7   softmax: thread r owns query row r (TMEM lane r): loads its
 //               128 scores with tcgen05.ld, applies the causal mask, updates
 //               the running max with lazy rescaling (O is rescaled in TMEM
-//               only when a row's max grows by more than 2^8), writes
-//               P = 2^(s - m) as fp16 into the swizzled P tile, and at the end
-//               divides O by the row sum and stores it.
+//               only when a row's max grows by more than 2^8), and writes
+//               P = 2^(s - m) over its own scores: fp16 pairs, head in
+//               columns [0,64) of the buffer and remainder in [64,128).  P(j)
+//               needs no wait on PV(j-1), which reads the other buffer; the
+//               MMAs of one thread run in issue order, so S(j+2) overwrites
+//               P(j) only after PV(j) has read it.  At the end the softmax
+//               warps divide O by the row sum and store it.
 // All waits are bounded; on expiry the kernel records
 // NWD_DEVERR_PIPE_TIMEOUT, lets its in-flight copies and MMAs land, frees its
 // TMEM and returns.
@@ -52,18 +59,17 @@ constexpr int KV_ST = 2;          // K/V ring stages
 constexpr int O_Q = 0;
 constexpr int O_K = O_Q + TILE;
 constexpr int O_V = O_K + KV_ST * TILE;
-constexpr int O_P = O_V + KV_ST * TILE;   // P head (fp16)
-constexpr int O_P2 = O_P + TILE;          // P remainder (fp16): p = head + remainder to ~22 bits
-constexpr int O_BAR = O_P2 + TILE;
-// barriers: q_full, kv_full[2], kv_empty[2], s_full, p_full, pv_done, drain
-constexpr int B_QFULL = 0, B_KVFULL = 1, B_KVEMPTY = 3, B_SFULL = 5, B_PFULL = 6, B_PVDONE = 7,
-              B_DRAIN = 8, NBAR = 9;
+constexpr int O_BAR = O_V + KV_ST * TILE;
+// barriers: q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full,
+// pv_done, drain
+constexpr int B_QFULL = 0, B_KFULL = 1, B_KEMPTY = 3, B_VFULL = 5, B_VEMPTY = 7, B_SFULL = 9,
+              B_PFULL = 11, B_PVDONE = 12, B_DRAIN = 13, NBAR = 14;
 constexpr int O_MISC = O_BAR + NBAR * 8;  // tmem base (u32), abort flag (i32)
 constexpr int P_SMEM_USED = O_MISC + 16;
 constexpr int P_SMEM_BYTES = P_SMEM_USED + 1024;
 static_assert(P_SMEM_BYTES <= 227 * 1024, "shared memory");
 
-constexpr uint32_t TMEM_COLS = 256;  // S [0,128), O [128,256)
+constexpr uint32_t TMEM_COLS = 512;  // S0 [0,128), S1 [128,256), O [256,384)
 constexpr float RESCALE_LOG2 = 8.f;
 
 struct PParams {
@@ -82,6 +88,17 @@ struct PParams {
 __device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
   return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
          ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+// A from tensor memory ([a] is a TMEM address: row i in lane i, fp16 pairs
+// along the columns), B from shared memory.
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
 // Instruction descriptor, kind::f16: fp32 accumulator (bits 4-5 = 1), fp16 A
 // and B (bits 7-12 = 0), A K-major, B K-major or MN-major (bit 16), N >> 3 in
@@ -175,10 +192,12 @@ __global__ void __launch_bounds__(PTHR, 1)
     *abort_flag = 0;
     mbar_init(bar + 8 * B_QFULL, 1);
     for (int s = 0; s < KV_ST; s++) {
-      mbar_init(bar + 8 * (B_KVFULL + s), 1);
-      mbar_init(bar + 8 * (B_KVEMPTY + s), 1);
+      mbar_init(bar + 8 * (B_KFULL + s), 1);
+      mbar_init(bar + 8 * (B_KEMPTY + s), 1);
+      mbar_init(bar + 8 * (B_VFULL + s), 1);
+      mbar_init(bar + 8 * (B_VEMPTY + s), 1);
+      mbar_init(bar + 8 * (B_SFULL + s), 1);
     }
-    mbar_init(bar + 8 * B_SFULL, 1);
     mbar_init(bar + 8 * B_PFULL, BM);
     mbar_init(bar + 8 * B_PVDONE, 1);
     mbar_init(bar + 8 * B_DRAIN, 1);
@@ -195,13 +214,13 @@ __global__ void __launch_bounds__(PTHR, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_s = tmem, tmem_o = tmem + 128;
+  const uint32_t tmem_o = tmem + 256;  // score buffers at tmem + 0 and tmem + 128
 
   if (warp == 0) {
     // ======================= TMA producer =======================
     const uint64_t pol_q = evict_first_policy(), pol_kv = evict_last_policy();
     const int kv_row0 = (int)p.row_offset[b];
-    uint32_t issued[KV_ST] = {0, 0};
+    uint32_t kissued[KV_ST] = {0, 0}, vissued[KV_ST] = {0, 0};
     bool q_issued = false, ok = true;
     if (lane == 0) {
       const uint32_t fb = bar + 8 * B_QFULL;
@@ -213,22 +232,34 @@ __global__ void __launch_bounds__(PTHR, 1)
     q_issued = true;
     __syncwarp();
     for (uint32_t j = 0; j < nblk && ok; j++) {
-      const uint32_t st = j & 1;
-      if (!warp_wait(bar + 8 * (B_KVEMPTY + st), ((j >> 1) & 1) ^ 1, abort_flag, &wsh->error)) {
+      const uint32_t st = j & 1, par = ((j >> 1) & 1) ^ 1;
+      const int row = kv_row0 + (int)(j * BN);
+      // K(j): its stage is free once S(j-2) has completed
+      if (!warp_wait(bar + 8 * (B_KEMPTY + st), par, abort_flag, &wsh->error)) {
         ok = false;
         break;
       }
       if (lane == 0) {
-        const uint32_t fb = bar + 8 * (B_KVFULL + st);
-        mbar_arrive_tx(fb, 2 * TILE);
-        const int row = kv_row0 + (int)(j * BN);
+        const uint32_t fb = bar + 8 * (B_KFULL + st);
+        mbar_arrive_tx(fb, TILE);
         tma_load_4d(sb + O_K + st * TILE, &tmk, fb, 0, 0, (int)hkv, row, pol_kv);
         tma_load_4d(sb + O_K + st * TILE + CHUNK, &tmk, fb, 0, 1, (int)hkv, row, pol_kv);
+      }
+      __syncwarp();
+      kissued[st]++;
+      // V(j): its stage is free once PV(j-2) has completed
+      if (!warp_wait(bar + 8 * (B_VEMPTY + st), par, abort_flag, &wsh->error)) {
+        ok = false;
+        break;
+      }
+      if (lane == 0) {
+        const uint32_t fb = bar + 8 * (B_VFULL + st);
+        mbar_arrive_tx(fb, TILE);
         tma_load_4d(sb + O_V + st * TILE, &tmv, fb, 0, 0, (int)hkv, row, pol_kv);
         tma_load_4d(sb + O_V + st * TILE + CHUNK, &tmv, fb, 0, 1, (int)hkv, row, pol_kv);
       }
       __syncwarp();
-      issued[st]++;
+      vissued[st]++;
     }
     if (!ok) {
       // let this CTA's copies in flight land before the CTA can exit
@@ -236,51 +267,67 @@ __global__ void __launch_bounds__(PTHR, 1)
       if (q_issued)
         while (!mbar_try_wait(bar + 8 * B_QFULL, 0) && globaltimer() - t0 < WAIT_LIMIT_NS) {
         }
-      for (int s = 0; s < KV_ST; s++)
-        if (issued[s])
-          while (!mbar_try_wait(bar + 8 * (B_KVFULL + s), (issued[s] - 1) & 1) &&
+      for (int s = 0; s < KV_ST; s++) {
+        if (kissued[s])
+          while (!mbar_try_wait(bar + 8 * (B_KFULL + s), (kissued[s] - 1) & 1) &&
                  globaltimer() - t0 < WAIT_LIMIT_NS) {
           }
+        if (vissued[s])
+          while (!mbar_try_wait(bar + 8 * (B_VFULL + s), (vissued[s] - 1) & 1) &&
+                 globaltimer() - t0 < WAIT_LIMIT_NS) {
+          }
+      }
     }
   } else if (warp == 1) {
     // ======================= MMA issuer =======================
     bool ok = warp_wait(bar + 8 * B_QFULL, 0, abort_flag, &wsh->error);
-    for (uint32_t j = 0; j < nblk && ok; j++) {
-      const uint32_t st = j & 1;
-      if (!warp_wait(bar + 8 * (B_KVFULL + st), (j >> 1) & 1, abort_flag, &wsh->error)) {
-        ok = false;
-        break;
-      }
+    // S(i) = Q K(i)^T into score buffer i & 1: 8 K-steps of 16 over head_dim
+    auto issue_s = [&](uint32_t i) -> bool {
+      const uint32_t st = i & 1;
+      if (!warp_wait(bar + 8 * (B_KFULL + st), (i >> 1) & 1, abort_flag, &wsh->error)) return false;
       tc_fence_after();
       if (lane == 0) {
-        // S = Q K^T: 8 K-steps of 16 over head_dim (4 per 64-column chunk)
 #pragma unroll
         for (int k = 0; k < 8; k++) {
           const uint32_t off = (uint32_t)(k >> 2) * CHUNK + (uint32_t)(k & 3) * 32;
-          umma(tmem_s, sdesc(sb + O_Q + off, 16, 1024), sdesc(sb + O_K + st * TILE + off, 16, 1024),
-               IDESC_S, k > 0);
+          umma(tmem + st * 128, sdesc(sb + O_Q + off, 16, 1024),
+               sdesc(sb + O_K + st * TILE + off, 16, 1024), IDESC_S, k > 0);
         }
-        umma_commit(bar + 8 * B_SFULL);
+        umma_commit(bar + 8 * (B_KEMPTY + st));
+        umma_commit(bar + 8 * (B_SFULL + st));
       }
       __syncwarp();
-      if (!warp_wait(bar + 8 * B_PFULL, j & 1, abort_flag, &wsh->error)) {
+      return true;
+    };
+    if (ok) ok = issue_s(0);
+    for (uint32_t j = 0; j < nblk && ok; j++) {
+      // one block ahead: S(j+1) overlaps the softmax of block j.  Its score
+      // buffer was last read by the softmax of block j-1, which finished
+      // before p_full(j-1) released PV(j-1) in the previous iteration.
+      if (j + 1 < nblk && !issue_s(j + 1)) {
+        ok = false;
+        break;
+      }
+      if (!warp_wait(bar + 8 * B_PFULL, j & 1, abort_flag, &wsh->error) ||
+          !warp_wait(bar + 8 * (B_VFULL + (j & 1)), (j >> 1) & 1, abort_flag, &wsh->error)) {
         ok = false;
         break;
       }
       tc_fence_after();
       if (lane == 0) {
-        // O += P V: 8 K-steps of 16 keys for the P head, then 8 for the P
-        // remainder; P K-major (keys contiguous), V MN-major (head_dim
+        // O += P V: 8 K-steps of 16 keys (8 TMEM columns of fp16 pairs)
+        // for the P head, then 8 for the P remainder; V MN-major (head_dim
         // contiguous): its 64-column chunks are LBO = 16 KiB apart
+        const uint32_t st = j & 1;
+        const uint32_t tmem_p = tmem + st * 128;
 #pragma unroll
         for (int k = 0; k < 16; k++) {
           const uint32_t kk = (uint32_t)(k & 7);
-          const uint32_t aoff = (k < 8 ? O_P : O_P2) + (kk >> 2) * CHUNK + (kk & 3) * 32;
-          umma(tmem_o, sdesc(sb + aoff, 16, 1024),
-               sdesc(sb + O_V + st * TILE + kk * 16 * 128, CHUNK, 1024), IDESC_O,
-               (j > 0 || k > 0) ? 1u : 0u);
+          umma_ts(tmem_o, tmem_p + (k < 8 ? 0u : 64u) + kk * 8u,
+                  sdesc(sb + O_V + st * TILE + kk * 16 * 128, CHUNK, 1024), IDESC_O,
+                  (j > 0 || k > 0) ? 1u : 0u);
         }
-        umma_commit(bar + 8 * (B_KVEMPTY + st));
+        umma_commit(bar + 8 * (B_VEMPTY + st));
         umma_commit(bar + 8 * B_PVDONE);
       }
       __syncwarp();
@@ -302,11 +349,12 @@ __global__ void __launch_bounds__(PTHR, 1)
     bool ok = true;
     float s[128];
     for (uint32_t j = 0; j < nblk; j++) {
-      if (!warp_wait(bar + 8 * B_SFULL, j & 1, abort_flag, &wsh->error)) {
+      if (!warp_wait(bar + 8 * (B_SFULL + (j & 1)), (j >> 1) & 1, abort_flag, &wsh->error)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      const uint32_t tmem_s = tmem + (j & 1) * 128;
 #pragma unroll
       for (int c = 0; c < 4; c++) tmem_ld32(tmem_s + lane_base + c * 32, s + c * 32);
       tmem_ld_wait();
@@ -321,14 +369,16 @@ __global__ void __launch_bounds__(PTHR, 1)
       for (int c = 0; c < 128; c++) mx = fmaxf(mx, s[c]);
       mx *= p.scale_log2;
       const bool up = mx > m + RESCALE_LOG2;
-      // P and O are in use by the previous PV until it completes
-      if (j > 0 && !warp_wait(bar + 8 * B_PVDONE, (j - 1) & 1, abort_flag, &wsh->error)) {
-        ok = false;
-        break;
-      }
       if (__any_sync(0xffffffffu, up)) {
         const float alpha = up ? ex2f(m - mx) : 1.f;  // 0 while m is -inf
         if (j > 0) {
+          // O is rescaled only after PV(j-1) has accumulated into it.  S(j)
+          // was issued after PV(j-2), so PV completions are j-1 or j here and
+          // the parity of phase j-1 is unambiguous.
+          if (!warp_wait(bar + 8 * B_PVDONE, (j - 1) & 1, abort_flag, &wsh->error)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           float ov[32];
 #pragma unroll
@@ -346,32 +396,32 @@ __global__ void __launch_bounds__(PTHR, 1)
       }
       const float nb = m == -INFINITY ? 0.f : -m;
       float rs = 0.f;
-      uint8_t* prow = smem + O_P + r * 128;
+      // P from the scores just read: the fp16 pair of scores 2c and 2c+1
+      // goes to head word c (stored over s[c], already consumed) and
+      // remainder word c
+      uint32_t* head = reinterpret_cast<uint32_t*>(s);
+      uint32_t rem[64];
 #pragma unroll
-      for (int u = 0; u < 16; u++) {  // 16-byte units: 8 keys each, chunk u / 8
-        uint32_t w[4], w2[4];
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const float p0 = ex2f(fmaf(s[u * 8 + 2 * e], p.scale_log2, nb));
-          const float p1 = ex2f(fmaf(s[u * 8 + 2 * e + 1], p.scale_log2, nb));
-          rs += p0 + p1;
-          __half2 hh = __floats2half2_rn(p0, p1);
-          __half2 rr = __floats2half2_rn(p0 - __low2float(hh), p1 - __high2float(hh));
-          w[e] = *reinterpret_cast<uint32_t*>(&hh);
-          w2[e] = *reinterpret_cast<uint32_t*>(&rr);
-        }
-        const uint32_t unit = (uint32_t)(u & 7) ^ (r & 7u);
-        *reinterpret_cast<uint4*>(prow + (u >> 3) * CHUNK + unit * 16) =
-            make_uint4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<uint4*>(prow + (O_P2 - O_P) + (u >> 3) * CHUNK + unit * 16) =
-            make_uint4(w2[0], w2[1], w2[2], w2[3]);
+      for (int c = 0; c < 64; c++) {
+        const float p0 = ex2f(fmaf(s[2 * c], p.scale_log2, nb));
+        const float p1 = ex2f(fmaf(s[2 * c + 1], p.scale_log2, nb));
+        rs += p0 + p1;
+        __half2 hh = __floats2half2_rn(p0, p1);
+        __half2 rr = __floats2half2_rn(p0 - __low2float(hh), p1 - __high2float(hh));
+        head[c] = *reinterpret_cast<uint32_t*>(&hh);
+        rem[c] = *reinterpret_cast<uint32_t*>(&rr);
       }
       l += rs;
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tmem_st32(tmem_s + lane_base, reinterpret_cast<float*>(head));
+      tmem_st32(tmem_s + lane_base + 32, reinterpret_cast<float*>(head + 32));
+      tmem_st32(tmem_s + lane_base + 64, reinterpret_cast<float*>(rem));
+      tmem_st32(tmem_s + lane_base + 96, reinterpret_cast<float*>(rem + 32));
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(bar + 8 * B_PFULL);
     }
-    if (ok && warp_wait(bar + 8 * B_PVDONE, (nblk - 1) & 1, abort_flag, &wsh->error)) {
+    // every PV has completed once the MMA warp's drain commit has arrived
+    if (ok && warp_wait(bar + 8 * B_DRAIN, 0, abort_flag, &wsh->error)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __half* orow = p.o + (((size_t)b * p.n_q + q0 + r) * p.n_heads + h) * PHD;
