@@ -6,32 +6,46 @@
 // cache row start_pos attends rows 0 .. start_pos + i.  This kernel computes
 // exactly that for a whole chunk at once, as a dense contraction.
 //
-// One CTA per (sequence, query head, 128-query tile), 8 warps:
-//   warp 0      TMA producer: the Q tile once, then K and V tiles of 128 rows
-//               into 2-stage rings with separate barriers (K(j) is free once
-//               S(j) is done, long before V(j)); each 128-row tile as two
-//               64-column chunks, 128-byte swizzle: the canonical K-major
-//               layout of the tcgen05 shared-memory descriptors.
-//   warp 1      MMA issuer (one thread): S(j) = Q K(j)^T into TMEM score
-//               buffer j & 1 (M=128 queries, N=128 keys, K=128 = 8 MMAs of
-//               K=16), issued one block ahead so it overlaps the softmax of
-//               block j-1; then, once P(j) is in TMEM, O += P V into TMEM
-//               columns [256,384) with A = P read from tensor memory and
-//               B = V an MN-major shared-memory operand.  P is an fp16 head
-//               and an fp16 remainder (16 MMAs): one fp16 rounding of P would
-//               exceed the parity tolerance on outputs near zero.
-//               tcgen05.commit signals S ready, K free, V free and PV done.
-//   warp 2      TMEM allocation (512 columns) and release.
-//   warps 4-7   softmax: thread r owns query row r (TMEM lane r): loads its
-//               128 scores with tcgen05.ld, applies the causal mask, updates
-//               the running max with lazy rescaling (O is rescaled in TMEM
-//               only when a row's max grows by more than 2^8), and writes
-//               P = 2^(s - m) over its own scores: fp16 pairs, head in
-//               columns [0,64) of the buffer and remainder in [64,128).  P(j)
-//               needs no wait on PV(j-1), which reads the other buffer; the
-//               MMAs of one thread run in issue order, so S(j+2) overwrites
-//               P(j) only after PV(j) has read it.  At the end the softmax
-//               warps divide O by the row sum and store it.
+// Work unit: a tile = (sequence, query head, 128 queries).  The kernel is
+// persistent: one CTA per SM walks the tiles heaviest first (late query tiles
+// see the most keys) in a snake order over the CTAs, and the roles below
+// stream from one tile into the next, so a tile's start (Q load, first scores)
+// and end (last P V, O read-out and store) overlap the neighbouring tiles'
+// work.  12 warps:
+//   warps 0, 3  TMA producers: warp 0 each tile's Q into one of two Q buffers
+//               and the K blocks of 128 rows, warp 3 the V blocks, each into
+//               a 2-stage ring (K(g) is free once S(g) is done, long before
+//               V(g)); each 128-row tile as two 64-column chunks, 128-byte
+//               swizzle: the canonical K-major layout of the tcgen05
+//               shared-memory descriptors.
+//   warp 1      MMA issuer (one thread).  Over the flattened sequence of
+//               blocks g of all its tiles: S(g) = Q K(g)^T into TMEM score
+//               buffer g & 1 (M=128 queries, N=128 keys, K=128 = 8 MMAs of
+//               K=16), up to one block ahead so it overlaps the softmax of
+//               block g-1; then, once P(g) is in TMEM, O += P V into the
+//               tile's TMEM accumulator (two, alternating by tile) with A = P
+//               read from tensor memory and B = V an MN-major shared-memory
+//               operand.  P is an fp16 head and an fp16 remainder (16 MMAs):
+//               one fp16 rounding of P would exceed the parity tolerance on
+//               outputs near zero.  tcgen05.commit signals S ready, K/V/Q
+//               free, PV done and O complete.
+//   warp 2      TMEM allocation (512 columns: S0, S1, O0, O1) and release.
+//   warps 4-7   softmax: thread r owns query row r (TMEM lane r).  Per block
+//               it reads its 128 scores (240 registers per thread: the other
+//               warpgroups give theirs up with setmaxnreg), applies the causal
+//               mask, updates the running max with lazy rescaling (O is
+//               rescaled in TMEM only when a row's max grows by more than
+//               2^8), and writes P = 2^(s - m) over its own scores as fp16
+//               pairs (per half: head, then remainder).  P(g) needs no wait on
+//               PV(g-1), which reads the other buffer; the MMAs of one thread
+//               run in issue order, so S(g+2) overwrites P(g) only after
+//               PV(g) has read it.  At the end of a tile it hands the row sums
+//               to the epilogue through shared memory.
+//   warps 8-11  epilogue: per tile, once its last PV has completed, divides
+//               O by the row sum and stores it as fp16, then frees the O
+//               buffer for the tile after next.
+// K/V rows past the chunk's end that a block covers are zeroed in shared
+// memory before P V reads them (P is 0 there, but 0 x NaN would not be).
 // All waits are bounded; on expiry the kernel records
 // NWD_DEVERR_PIPE_TIMEOUT, lets its in-flight copies and MMAs land, frees its
 // TMEM and returns.
@@ -51,25 +65,32 @@ using nwd::WsHeader;
 constexpr int PHD = 128;          // head_dim
 constexpr int BM = 128;           // queries per tile
 constexpr int BN = 128;           // keys per block
-constexpr int PTHR = 256;         // 8 warps
+constexpr int PTHR = 384;         // 12 warps
 constexpr int CHUNK = 128 * 128;  // 128 rows x 64 fp16 (one 64-column chunk): 16 KiB
 constexpr int TILE = 2 * CHUNK;   // 128 x 128 fp16: 32 KiB
-constexpr int KV_ST = 2;          // K/V ring stages
 
-constexpr int O_Q = 0;
-constexpr int O_K = O_Q + TILE;
-constexpr int O_V = O_K + KV_ST * TILE;
-constexpr int O_BAR = O_V + KV_ST * TILE;
-// barriers: q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full,
-// pv_done, drain
-constexpr int B_QFULL = 0, B_KFULL = 1, B_KEMPTY = 3, B_VFULL = 5, B_VEMPTY = 7, B_SFULL = 9,
-              B_PFULL = 11, B_PVDONE = 12, B_DRAIN = 13, NBAR = 14;
+constexpr int O_Q = 0;                  // 2 Q buffers
+constexpr int O_K = O_Q + 2 * TILE;     // 2 K stages
+constexpr int O_V = O_K + 2 * TILE;     // 2 V stages
+constexpr int O_L = O_V + 2 * TILE;     // row sums handed to the epilogue [2][128] f32
+constexpr int O_BAR = O_L + 2 * BM * 4;
+// barrier pairs are indexed by buffer (Q, O, L: tile parity; K, V, S, P: block parity)
+// Pairs: Q, L by tile parity; K, V by block parity.  Triples: S, P and PV
+// done by score buffer (block index mod 3).  V_TMA: completion of a V copy
+// whose rows past the chunk's end are zeroed before V_FULL (the producer
+// waits for each such copy before it issues the next).
+constexpr int B_QFULL = 0, B_QEMPTY = 2, B_KFULL = 4, B_KEMPTY = 6, B_VFULL = 8, B_VEMPTY = 10,
+              B_VTMA = 12, B_LFULL = 13, B_LEMPTY = 15, B_SFULL = 17, B_PFULL = 20,
+              B_PVDONE = 23, B_OFULL = 26, B_OEMPTY = 27, B_DRAIN = 28, NBAR = 29;
 constexpr int O_MISC = O_BAR + NBAR * 8;  // tmem base (u32), abort flag (i32)
 constexpr int P_SMEM_USED = O_MISC + 16;
 constexpr int P_SMEM_BYTES = P_SMEM_USED + 1024;
 static_assert(P_SMEM_BYTES <= 227 * 1024, "shared memory");
 
-constexpr uint32_t TMEM_COLS = 512;  // S0 [0,128), S1 [128,256), O [256,384)
+constexpr uint32_t TMEM_COLS = 512;  // S0, S1, S2 (128 columns each), then O at 384
+constexpr uint32_t TMEM_O = 384;
+constexpr uint32_t NSBUF = 3;        // score / P buffers
+constexpr uint32_t GROUP_THREADS = 128;  // softmax / epilogue warpgroups
 constexpr float RESCALE_LOG2 = 8.f;
 
 struct PParams {
@@ -77,9 +98,33 @@ struct PParams {
   const int64_t* row_offset;
   uint8_t* ws;
   uint64_t pool_rows;
-  uint32_t batch, n_q, start_pos, n_heads, n_kv, group, q_tiles;
+  uint32_t batch, n_q, start_pos, n_heads, n_kv, group, q_tiles, n_tiles;
   float scale_log2;
 };
+
+// One tile of the heaviest-first snake schedule: round k of CTA c takes tile
+// k * G + c (k even) or k * G + G - 1 - c (k odd); tile index t covers query
+// tile q_tiles - 1 - t / (batch * n_heads) of (sequence, head) t % (batch * n_heads).
+struct Tile {
+  uint32_t b, h, hkv, q0, nq, nblk;
+  int kv_row0;
+};
+__device__ __forceinline__ bool get_tile(const PParams& p, uint32_t k, Tile& t) {
+  const uint32_t G = gridDim.x, c = blockIdx.x;
+  const uint64_t idx = (uint64_t)k * G + ((k & 1u) ? (G - 1 - c) : c);
+  if (idx >= p.n_tiles) return false;
+  const uint32_t bh_count = p.batch * p.n_heads;
+  const uint32_t rank = (uint32_t)(idx / bh_count), bh = (uint32_t)(idx % bh_count);
+  const uint32_t qt = p.q_tiles - 1 - rank;
+  t.b = bh / p.n_heads;
+  t.h = bh % p.n_heads;
+  t.hkv = t.h / p.group;
+  t.q0 = qt * BM;
+  t.nq = min((uint32_t)BM, p.n_q - t.q0);
+  t.nblk = (p.start_pos + t.q0 + t.nq - 1) / BN + 1;  // causal horizon of the tile
+  t.kv_row0 = (int)p.row_offset[t.b];
+  return true;
+}
 
 // ---- tcgen05 wrappers ----
 // Shared-memory matrix descriptor: start address, leading / stride byte
@@ -166,6 +211,39 @@ __device__ __forceinline__ float ex2f(float x) {
   return y;
 }
 
+// P for one half row: the fp16 pair of scores 2c and 2c+1 becomes head word
+// c and remainder word c; they are written back over the half's own score
+// columns (head at +0, remainder at +32).  Returns the half's sum of P.
+__device__ __forceinline__ float store_p_half(uint32_t taddr, float* s, float scale_log2,
+                                              float nb) {
+  float rsv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float head[32], rem[32];
+#pragma unroll
+  for (int c = 0; c < 32; c++) {
+    const float p0 = ex2f(fmaf(s[2 * c], scale_log2, nb));
+    const float p1 = ex2f(fmaf(s[2 * c + 1], scale_log2, nb));
+    rsv[c & 7] += p0 + p1;
+    __half2 hh = __floats2half2_rn(p0, p1);
+    __half2 rr = __floats2half2_rn(p0 - __low2float(hh), p1 - __high2float(hh));
+    head[c] = __uint_as_float(*reinterpret_cast<uint32_t*>(&hh));
+    rem[c] = __uint_as_float(*reinterpret_cast<uint32_t*>(&rr));
+  }
+  tmem_st32(taddr, head);
+  tmem_st32(taddr + 32, rem);
+  return ((rsv[0] + rsv[4]) + (rsv[1] + rsv[5])) + ((rsv[2] + rsv[6]) + (rsv[3] + rsv[7]));
+}
+
+// Position in a ring of 3 buffers: the buffer and the parity of its use.
+struct Ring3 {
+  uint32_t buf = 0, phase = 0;
+  __device__ __forceinline__ void next() {
+    if (++buf == NSBUF) {
+      buf = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
 __global__ void __launch_bounds__(PTHR, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                    const __grid_constant__ CUtensorMap tmv, const __grid_constant__ PParams p) {
@@ -177,29 +255,28 @@ __global__ void __launch_bounds__(PTHR, 1)
   volatile int32_t* abort_flag = reinterpret_cast<int32_t*>(smem + O_MISC + 4);
   WsHeader* wsh = reinterpret_cast<WsHeader*>(p.ws);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-
-  // heavy tiles (late queries see the most keys) get the lowest block indices
-  const uint32_t bh_count = p.batch * p.n_heads;
-  const uint32_t tile_rank = blockIdx.x / bh_count, bh = blockIdx.x % bh_count;
-  const uint32_t qt = p.q_tiles - 1 - tile_rank;
-  const uint32_t b = bh / p.n_heads, h = bh % p.n_heads, hkv = h / p.group;
-  const uint32_t q0 = qt * BM;
-  const uint32_t nq_valid = min((uint32_t)BM, p.n_q - q0);
-  const uint32_t last_key = p.start_pos + q0 + nq_valid - 1;  // causal horizon of the tile
-  const uint32_t nblk = last_key / BN + 1;
+  const uint32_t key_end = p.start_pos + p.n_q;  // rows past the chunk are never valid
 
   if (tid == 0) {
     *abort_flag = 0;
-    mbar_init(bar + 8 * B_QFULL, 1);
-    for (int s = 0; s < KV_ST; s++) {
+    for (int s = 0; s < 2; s++) {
+      mbar_init(bar + 8 * (B_QFULL + s), 1);
+      mbar_init(bar + 8 * (B_QEMPTY + s), 1);
       mbar_init(bar + 8 * (B_KFULL + s), 1);
       mbar_init(bar + 8 * (B_KEMPTY + s), 1);
       mbar_init(bar + 8 * (B_VFULL + s), 1);
       mbar_init(bar + 8 * (B_VEMPTY + s), 1);
-      mbar_init(bar + 8 * (B_SFULL + s), 1);
+      mbar_init(bar + 8 * (B_LFULL + s), GROUP_THREADS);
+      mbar_init(bar + 8 * (B_LEMPTY + s), GROUP_THREADS);
     }
-    mbar_init(bar + 8 * B_PFULL, BM);
-    mbar_init(bar + 8 * B_PVDONE, 1);
+    for (int s = 0; s < (int)NSBUF; s++) {
+      mbar_init(bar + 8 * (B_SFULL + s), 1);
+      mbar_init(bar + 8 * (B_PFULL + s), GROUP_THREADS);
+      mbar_init(bar + 8 * (B_PVDONE + s), 1);
+    }
+    mbar_init(bar + 8 * B_VTMA, 1);
+    mbar_init(bar + 8 * B_OFULL, 1);
+    mbar_init(bar + 8 * B_OEMPTY, GROUP_THREADS);
     mbar_init(bar + 8 * B_DRAIN, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -214,237 +291,341 @@ __global__ void __launch_bounds__(PTHR, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_o = tmem + 256;  // score buffers at tmem + 0 and tmem + 128
-
-  if (warp == 0) {
-    // ======================= TMA producer =======================
+  // Register split (per thread), set at the top of each role: producer/MMA
+  // warpgroup 56, softmax 240, epilogue 120.  128 * (56 + 240 + 120) = 53248
+  // registers, within the 384 * 168 = 64512 this kernel is launched with.
+  if (warp == 0 || warp == 3) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
+    // ================ TMA producers: warp 0 Q and K, warp 3 V ================
+    // K and V come from separate warps so that K(g+1), needed early for the
+    // look-ahead S, never queues behind V(g), whose stage frees only when
+    // PV(g-2) completes.
+    const bool kq = warp == 0;
     const uint64_t pol_q = evict_first_policy(), pol_kv = evict_last_policy();
-    const int kv_row0 = (int)p.row_offset[b];
-    uint32_t kissued[KV_ST] = {0, 0}, vissued[KV_ST] = {0, 0};
-    bool q_issued = false, ok = true;
-    if (lane == 0) {
-      const uint32_t fb = bar + 8 * B_QFULL;
-      mbar_arrive_tx(fb, TILE);
-      const int qrow = (int)(b * p.n_q + q0);
-      tma_load_4d(sb + O_Q, &tmq, fb, 0, 0, (int)h, qrow, pol_q);
-      tma_load_4d(sb + O_Q + CHUNK, &tmq, fb, 0, 1, (int)h, qrow, pol_q);
-    }
-    q_issued = true;
-    __syncwarp();
-    for (uint32_t j = 0; j < nblk && ok; j++) {
-      const uint32_t st = j & 1, par = ((j >> 1) & 1) ^ 1;
-      const int row = kv_row0 + (int)(j * BN);
-      // K(j): its stage is free once S(j-2) has completed
-      if (!warp_wait(bar + 8 * (B_KEMPTY + st), par, abort_flag, &wsh->error)) {
-        ok = false;
-        break;
+    // loads issued so far (buffer i of a pair got the ones with index parity i)
+    uint32_t nq = 0, nkv = 0, ntma = 0;
+    bool ok = true;
+    uint32_t g = 0, u = 0;
+    Tile t;
+    const int kv_full = kq ? B_KFULL : B_VFULL, kv_empty = kq ? B_KEMPTY : B_VEMPTY;
+    const uint32_t kv_smem = sb + (kq ? O_K : O_V);
+    const CUtensorMap* kv_map = kq ? &tmk : &tmv;
+    for (uint32_t k = 0; ok && get_tile(p, k, t); k++, u++) {
+      if (kq) {
+        const uint32_t qs = u & 1;
+        // Q buffer qs is free once the last S of tile u-2 has completed
+        if (!warp_wait(bar + 8 * (B_QEMPTY + qs), ((u >> 1) & 1) ^ 1, abort_flag, &wsh->error)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          const uint32_t fb = bar + 8 * (B_QFULL + qs);
+          mbar_arrive_tx(fb, TILE);
+          const int qrow = (int)(t.b * p.n_q + t.q0);
+          tma_load_4d(sb + O_Q + qs * TILE, &tmq, fb, 0, 0, (int)t.h, qrow, pol_q);
+          tma_load_4d(sb + O_Q + qs * TILE + CHUNK, &tmq, fb, 0, 1, (int)t.h, qrow, pol_q);
+        }
+        __syncwarp();
+        nq++;
       }
-      if (lane == 0) {
-        const uint32_t fb = bar + 8 * (B_KFULL + st);
-        mbar_arrive_tx(fb, TILE);
-        tma_load_4d(sb + O_K + st * TILE, &tmk, fb, 0, 0, (int)hkv, row, pol_kv);
-        tma_load_4d(sb + O_K + st * TILE + CHUNK, &tmk, fb, 0, 1, (int)hkv, row, pol_kv);
+      for (uint32_t j = 0; j < t.nblk; j++, g++) {
+        const uint32_t st = g & 1;
+        // K(g) is free once S(g-2) has completed, V(g) once PV(g-2) has
+        if (!warp_wait(bar + 8 * (kv_empty + st), ((g >> 1) & 1) ^ 1, abort_flag,
+                       &wsh->error)) {
+          ok = false;
+          break;
+        }
+        const int row = t.kv_row0 + (int)(j * BN);
+        // V rows past the chunk's end (P is 0 there, but 0 x NaN would not
+        // be): the copy completes on V_TMA, this warp zeroes them, then
+        // releases the stage on V_FULL
+        const uint32_t valid = key_end - j * BN;
+        const bool tail = !kq && valid < (uint32_t)BN;
+        const uint32_t fb = bar + 8 * (tail ? B_VTMA : kv_full + st);
+        if (lane == 0) {
+          mbar_arrive_tx(fb, TILE);
+          tma_load_4d(kv_smem + st * TILE, kv_map, fb, 0, 0, (int)t.hkv, row, pol_kv);
+          tma_load_4d(kv_smem + st * TILE + CHUNK, kv_map, fb, 0, 1, (int)t.hkv, row, pol_kv);
+        }
+        __syncwarp();
+        if (tail) {
+          ntma++;
+          if (!warp_wait(fb, (ntma - 1) & 1, abort_flag, &wsh->error)) {
+            ok = false;
+            break;
+          }
+          // rows [valid, 128) of both 64-column chunks: 128 bytes each
+          const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+          for (uint32_t i = valid * 8 + (uint32_t)lane; i < (uint32_t)BN * 8; i += 32) {
+            reinterpret_cast<uint4*>(smem + O_V + st * TILE)[i] = z;
+            reinterpret_cast<uint4*>(smem + O_V + st * TILE + CHUNK)[i] = z;
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar + 8 * (kv_full + st));
+        }
+        nkv++;
       }
-      __syncwarp();
-      kissued[st]++;
-      // V(j): its stage is free once PV(j-2) has completed
-      if (!warp_wait(bar + 8 * (B_VEMPTY + st), par, abort_flag, &wsh->error)) {
-        ok = false;
-        break;
-      }
-      if (lane == 0) {
-        const uint32_t fb = bar + 8 * (B_VFULL + st);
-        mbar_arrive_tx(fb, TILE);
-        tma_load_4d(sb + O_V + st * TILE, &tmv, fb, 0, 0, (int)hkv, row, pol_kv);
-        tma_load_4d(sb + O_V + st * TILE + CHUNK, &tmv, fb, 0, 1, (int)hkv, row, pol_kv);
-      }
-      __syncwarp();
-      vissued[st]++;
     }
     if (!ok) {
-      // let this CTA's copies in flight land before the CTA can exit
+      // let this warp's copies in flight land before the CTA can exit
       const uint64_t t0 = globaltimer();
-      if (q_issued)
-        while (!mbar_try_wait(bar + 8 * B_QFULL, 0) && globaltimer() - t0 < WAIT_LIMIT_NS) {
+      auto land = [&](int base, uint32_t n) {
+#pragma unroll
+        for (uint32_t s = 0; s < 2; s++) {
+          const uint32_t cnt = (n + 1 - s) / 2;  // loads that went to buffer s
+          if (cnt)
+            while (!mbar_try_wait(bar + 8 * (base + s), (cnt - 1) & 1) &&
+                   globaltimer() - t0 < WAIT_LIMIT_NS) {
+            }
         }
-      for (int s = 0; s < KV_ST; s++) {
-        if (kissued[s])
-          while (!mbar_try_wait(bar + 8 * (B_KFULL + s), (kissued[s] - 1) & 1) &&
-                 globaltimer() - t0 < WAIT_LIMIT_NS) {
-          }
-        if (vissued[s])
-          while (!mbar_try_wait(bar + 8 * (B_VFULL + s), (vissued[s] - 1) & 1) &&
+      };
+      if (kq) {
+        land(B_QFULL, nq);
+        land(B_KFULL, nkv);
+      } else {
+        // a V copy completes on V_FULL (counted by nkv once released) or, for
+        // a tail block, on V_TMA (its last phase covers one still in flight)
+        land(B_VFULL, nkv);
+        if (ntma)
+          while (!mbar_try_wait(bar + 8 * B_VTMA, (ntma - 1) & 1) &&
                  globaltimer() - t0 < WAIT_LIMIT_NS) {
           }
       }
     }
   } else if (warp == 1) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");
     // ======================= MMA issuer =======================
-    bool ok = warp_wait(bar + 8 * B_QFULL, 0, abort_flag, &wsh->error);
-    // S(i) = Q K(i)^T into score buffer i & 1: 8 K-steps of 16 over head_dim
-    auto issue_s = [&](uint32_t i) -> bool {
-      const uint32_t st = i & 1;
-      if (!warp_wait(bar + 8 * (B_KFULL + st), (i >> 1) & 1, abort_flag, &wsh->error)) return false;
-      tc_fence_after();
-      if (lane == 0) {
+    // Over the flattened blocks of all its tiles, the issuer polls for the
+    // next S and the next PV and issues whichever is ready, S first:
+    //   S(gs)  needs K(gs) (and the tile's Q at its first block) and
+    //          gs <= gp + 2, i.e. PV(gs-3), which reads P from the score
+    //          buffer S(gs) overwrites, already issued (the MMAs of one
+    //          thread run in order);
+    //   PV(gp) needs gp < gs, P(gp) and V(gp), and at a tile's first block
+    //          the O accumulator released by the epilogue.
+    // S thus runs up to two blocks ahead of PV: the softmax of a block never
+    // waits for the PV two blocks back.
+    // The scheduler runs on lane 0 alone (an MMA issue blocks while the
+    // tensor pipe's queue is full, so every cycle between issues is idle
+    // tensor time): no warp-collective operation in the loop, and the clock
+    // is read only while nothing can be issued.
+    if (lane == 0) {
+      Tile ts, tp;
+      uint32_t ks = 0, us = 0, js = 0, gs = 0;  // next S
+      uint32_t kp = 0, up = 0, jp = 0, gp = 0;  // next PV
+      Ring3 rs, rp;                             // their score buffers
+      bool have_s = get_tile(p, 0, ts);
+      bool have_p = get_tile(p, 0, tp);
+      uint32_t idle = 0;
+      uint64_t idle_since = 0;
+      while (have_p) {
+        if (have_s && gs <= gp + 2 &&
+            (js != 0 || mbar_test_wait(bar + 8 * (B_QFULL + (us & 1)), (us >> 1) & 1)) &&
+            mbar_test_wait(bar + 8 * (B_KFULL + (gs & 1)), (gs >> 1) & 1)) {
+          const uint32_t st = gs & 1, qs = us & 1;
+          tc_fence_after();
+          // 8 K-steps of 16 over head_dim (32 bytes apart in a 64-column chunk)
+          const uint64_t da = sdesc(sb + O_Q + qs * TILE, 16, 1024);
+          const uint64_t db = sdesc(sb + O_K + st * TILE, 16, 1024);
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
-          const uint32_t off = (uint32_t)(k >> 2) * CHUNK + (uint32_t)(k & 3) * 32;
-          umma(tmem + st * 128, sdesc(sb + O_Q + off, 16, 1024),
-               sdesc(sb + O_K + st * TILE + off, 16, 1024), IDESC_S, k > 0);
-        }
-        umma_commit(bar + 8 * (B_KEMPTY + st));
-        umma_commit(bar + 8 * (B_SFULL + st));
-      }
-      __syncwarp();
-      return true;
-    };
-    if (ok) ok = issue_s(0);
-    for (uint32_t j = 0; j < nblk && ok; j++) {
-      // one block ahead: S(j+1) overlaps the softmax of block j.  Its score
-      // buffer was last read by the softmax of block j-1, which finished
-      // before p_full(j-1) released PV(j-1) in the previous iteration.
-      if (j + 1 < nblk && !issue_s(j + 1)) {
-        ok = false;
-        break;
-      }
-      if (!warp_wait(bar + 8 * B_PFULL, j & 1, abort_flag, &wsh->error) ||
-          !warp_wait(bar + 8 * (B_VFULL + (j & 1)), (j >> 1) & 1, abort_flag, &wsh->error)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      if (lane == 0) {
-        // O += P V: 8 K-steps of 16 keys (8 TMEM columns of fp16 pairs)
-        // for the P head, then 8 for the P remainder; V MN-major (head_dim
-        // contiguous): its 64-column chunks are LBO = 16 KiB apart
-        const uint32_t st = j & 1;
-        const uint32_t tmem_p = tmem + st * 128;
+          for (int kk = 0; kk < 8; kk++) {
+            // the start address field is addr >> 4: offsets add directly
+            const uint32_t off = ((uint32_t)(kk >> 2) * CHUNK + (uint32_t)(kk & 3) * 32) >> 4;
+            umma(tmem + rs.buf * 128, da + off, db + off, IDESC_S, kk > 0);
+          }
+          umma_commit(bar + 8 * (B_KEMPTY + st));
+          umma_commit(bar + 8 * (B_SFULL + rs.buf));
+          if (js + 1 == ts.nblk) umma_commit(bar + 8 * (B_QEMPTY + qs));
+          gs++;
+          rs.next();
+          if (++js == ts.nblk) {
+            js = 0;
+            us++;
+            have_s = get_tile(p, ++ks, ts);
+          }
+          idle = 0;
+        } else if (gp < gs && (jp != 0 || mbar_test_wait(bar + 8 * B_OEMPTY, (up & 1) ^ 1)) &&
+                   mbar_test_wait(bar + 8 * (B_PFULL + rp.buf), rp.phase) &&
+                   mbar_test_wait(bar + 8 * (B_VFULL + (gp & 1)), (gp >> 1) & 1)) {
+          const uint32_t st = gp & 1;
+          tc_fence_after();
+          // O += P V: 8 K-steps of 16 keys (8 TMEM columns of fp16 pairs) for
+          // the P head, then 8 for the P remainder.  P columns: keys [0,64)
+          // head at +0 and remainder at +32, keys [64,128) head at +64 and
+          // remainder at +96.  V MN-major (head_dim contiguous): its
+          // 64-column chunks are LBO = 16 KiB apart; 16 keys are 2 KiB.
+          const uint32_t tmem_p = tmem + rp.buf * 128;
+          const uint64_t dv = sdesc(sb + O_V + st * TILE, CHUNK, 1024);
 #pragma unroll
-        for (int k = 0; k < 16; k++) {
-          const uint32_t kk = (uint32_t)(k & 7);
-          umma_ts(tmem_o, tmem_p + (k < 8 ? 0u : 64u) + kk * 8u,
-                  sdesc(sb + O_V + st * TILE + kk * 16 * 128, CHUNK, 1024), IDESC_O,
-                  (j > 0 || k > 0) ? 1u : 0u);
+          for (int kstep = 0; kstep < 16; kstep++) {
+            const uint32_t kk = (uint32_t)(kstep & 7);
+            umma_ts(tmem + TMEM_O,
+                    tmem_p + (kk >> 2) * 64u + (kstep < 8 ? 0u : 32u) + (kk & 3u) * 8u,
+                    dv + ((kk * 16 * 128) >> 4), IDESC_O, (jp > 0 || kstep > 0) ? 1u : 0u);
+          }
+          umma_commit(bar + 8 * (B_VEMPTY + st));
+          umma_commit(bar + 8 * (B_PVDONE + rp.buf));
+          if (jp + 1 == tp.nblk) umma_commit(bar + 8 * B_OFULL);
+          gp++;
+          rp.next();
+          if (++jp == tp.nblk) {
+            jp = 0;
+            up++;
+            have_p = get_tile(p, ++kp, tp);
+          }
+          idle = 0;
+        } else if ((++idle & 63) == 0) {
+          // nothing ready: give up after WAIT_LIMIT_NS without progress
+          if (*abort_flag) break;
+          const uint64_t now = globaltimer();
+          if (idle == 64) {
+            idle_since = now;
+          } else if (now - idle_since > WAIT_LIMIT_NS) {
+            atomicOr(&wsh->error, NWD_DEVERR_PIPE_TIMEOUT);
+            *abort_flag = 1;
+            break;
+          }
         }
-        umma_commit(bar + 8 * (B_VEMPTY + st));
-        umma_commit(bar + 8 * B_PVDONE);
       }
-      __syncwarp();
     }
+    __syncwarp();
     // every MMA this thread issued has completed before TMEM is released
     if (lane == 0) umma_commit(bar + 8 * B_DRAIN);
     __syncwarp();
     const uint64_t t0 = globaltimer();
     while (!mbar_try_wait(bar + 8 * B_DRAIN, 0) && globaltimer() - t0 < WAIT_LIMIT_NS) {
     }
-  } else if (warp >= 4) {
-    // ======================= softmax / epilogue =======================
-    const uint32_t r = (uint32_t)(tid - 128);          // query row = TMEM lane
+  } else if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;" ::: "memory");  // TMEM owner, idle
+  } else if (warp < 8) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 240;" ::: "memory");
+    // ======================= softmax =======================
+    const uint32_t r = (uint32_t)(tid - 128);                 // query row = TMEM lane
     const uint32_t lane_base = (uint32_t)(warp - 4) * 32u << 16;
-    const uint32_t qpos = p.start_pos + q0 + r;          // this row's last visible key
-    const uint32_t key_end = p.start_pos + p.n_q;        // rows past the chunk are never valid
-    const uint32_t horizon = min(qpos, key_end - 1);
-    float m = -INFINITY, l = 0.f;
+    const uint32_t tmem_o = tmem + TMEM_O + lane_base;
+    float* lsum = reinterpret_cast<float*>(smem + O_L);
     bool ok = true;
+    uint32_t u = 0;
+    Ring3 rb;        // score buffer of the current block
+    Ring3 rprev;     // score buffer of the block before it
+    Tile t;
     float s[128];
-    for (uint32_t j = 0; j < nblk; j++) {
-      if (!warp_wait(bar + 8 * (B_SFULL + (j & 1)), (j >> 1) & 1, abort_flag, &wsh->error)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t tmem_s = tmem + (j & 1) * 128;
-#pragma unroll
-      for (int c = 0; c < 4; c++) tmem_ld32(tmem_s + lane_base + c * 32, s + c * 32);
-      tmem_ld_wait();
-      const uint32_t key0 = j * BN;
-      if (key0 + BN - 1 > horizon) {
-#pragma unroll
-        for (int c = 0; c < 128; c++)
-          if (key0 + c > horizon) s[c] = -INFINITY;
-      }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 128; c++) mx = fmaxf(mx, s[c]);
-      mx *= p.scale_log2;
-      const bool up = mx > m + RESCALE_LOG2;
-      if (__any_sync(0xffffffffu, up)) {
-        const float alpha = up ? ex2f(m - mx) : 1.f;  // 0 while m is -inf
-        if (j > 0) {
-          // O is rescaled only after PV(j-1) has accumulated into it.  S(j)
-          // was issued after PV(j-2), so PV completions are j-1 or j here and
-          // the parity of phase j-1 is unambiguous.
-          if (!warp_wait(bar + 8 * B_PVDONE, (j - 1) & 1, abort_flag, &wsh->error)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          float ov[32];
-#pragma unroll
-          for (int c = 0; c < 4; c++) {
-            tmem_ld32(tmem_o + lane_base + c * 32, ov);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; i++) ov[i] *= alpha;
-            tmem_st32(tmem_o + lane_base + c * 32, ov);
-          }
-          tmem_st_wait();
+    for (uint32_t k = 0; ok && get_tile(p, k, t); k++, u++) {
+      const uint32_t horizon = min(p.start_pos + t.q0 + r, key_end - 1);
+      float m = -INFINITY, l = 0.f;
+      for (uint32_t j = 0; j < t.nblk; j++) {
+        if (!warp_wait(bar + 8 * (B_SFULL + rb.buf), rb.phase, abort_flag, &wsh->error)) {
+          ok = false;
+          break;
         }
-        l *= alpha;
-        if (up) m = mx;
-      }
-      const float nb = m == -INFINITY ? 0.f : -m;
-      float rs = 0.f;
-      // P from the scores just read: the fp16 pair of scores 2c and 2c+1
-      // goes to head word c (stored over s[c], already consumed) and
-      // remainder word c
-      uint32_t* head = reinterpret_cast<uint32_t*>(s);
-      uint32_t rem[64];
+        tc_fence_after();
+        const uint32_t tmem_s = tmem + rb.buf * 128 + lane_base;
+        const uint32_t key0 = j * BN;
 #pragma unroll
-      for (int c = 0; c < 64; c++) {
-        const float p0 = ex2f(fmaf(s[2 * c], p.scale_log2, nb));
-        const float p1 = ex2f(fmaf(s[2 * c + 1], p.scale_log2, nb));
-        rs += p0 + p1;
-        __half2 hh = __floats2half2_rn(p0, p1);
-        __half2 rr = __floats2half2_rn(p0 - __low2float(hh), p1 - __high2float(hh));
-        head[c] = *reinterpret_cast<uint32_t*>(&hh);
-        rem[c] = *reinterpret_cast<uint32_t*>(&rr);
+        for (int c = 0; c < 4; c++) tmem_ld32(tmem_s + c * 32, s + c * 32);
+        tmem_ld_wait();
+        if (key0 + BN - 1 > horizon) {
+#pragma unroll
+          for (int c = 0; c < 128; c++)
+            if (key0 + c > horizon) s[c] = -INFINITY;
+        }
+        // eight independent max chains, then a tree
+        float mv[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) mv[i] = s[i];
+#pragma unroll
+        for (int c = 8; c < 128; c++) mv[c & 7] = fmaxf(mv[c & 7], s[c]);
+#pragma unroll
+        for (int i = 0; i < 4; i++) mv[i] = fmaxf(mv[i], mv[i + 4]);
+        const float mx = fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3])) * p.scale_log2;
+        const bool up = mx > m + RESCALE_LOG2;
+        if (__any_sync(0xffffffffu, up)) {
+          const float alpha = up ? ex2f(m - mx) : 1.f;  // 0 while m is -inf
+          if (j > 0) {
+            // O is rescaled only after PV of the block before has accumulated
+            // into it.  Its PV_DONE barrier (one per score buffer) last
+            // completed for the block three before that, which finished
+            // before S of this block was issued: the parity is unambiguous.
+            if (!warp_wait(bar + 8 * (B_PVDONE + rprev.buf), rprev.phase, abort_flag,
+                           &wsh->error)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            float ov[32];
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+              tmem_ld32(tmem_o + c * 32, ov);
+              tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 32; i++) ov[i] *= alpha;
+              tmem_st32(tmem_o + c * 32, ov);
+            }
+          }
+          l *= alpha;
+          if (up) m = mx;
+        }
+        const float nb = m == -INFINITY ? 0.f : -m;
+        l += store_p_half(tmem_s, s, p.scale_log2, nb) +
+             store_p_half(tmem_s + 64, s + 64, p.scale_log2, nb);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(bar + 8 * (B_PFULL + rb.buf));
+        rprev = rb;
+        rb.next();
       }
-      l += rs;
-      tmem_st32(tmem_s + lane_base, reinterpret_cast<float*>(head));
-      tmem_st32(tmem_s + lane_base + 32, reinterpret_cast<float*>(head + 32));
-      tmem_st32(tmem_s + lane_base + 64, reinterpret_cast<float*>(rem));
-      tmem_st32(tmem_s + lane_base + 96, reinterpret_cast<float*>(rem + 32));
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(bar + 8 * B_PFULL);
+      if (!ok) break;
+      // hand the row sums of tile u to the epilogue
+      const uint32_t ls = u & 1;
+      if (!warp_wait(bar + 8 * (B_LEMPTY + ls), ((u >> 1) & 1) ^ 1, abort_flag, &wsh->error))
+        break;
+      lsum[ls * BM + r] = l;
+      mbar_arrive(bar + 8 * (B_LFULL + ls));
     }
-    // every PV has completed once the MMA warp's drain commit has arrived
-    if (ok && warp_wait(bar + 8 * B_DRAIN, 0, abort_flag, &wsh->error)) {
+  } else {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 120;" ::: "memory");
+    // ======================= epilogue =======================
+    // Per tile: once its last PV has completed, O is read out of TMEM as
+    // fp16 (normalised by the row sum) and the accumulator is released for
+    // the next tile's first PV before the rows are stored.
+    const uint32_t quad = (uint32_t)warp & 3u;
+    const uint32_t r = quad * 32u + (uint32_t)lane;
+    const uint32_t lane_base = quad * 32u << 16;
+    const float* lsum = reinterpret_cast<const float*>(smem + O_L);
+    uint32_t u = 0;
+    Tile t;
+    for (uint32_t k = 0; get_tile(p, k, t); k++, u++) {
+      const uint32_t ls = u & 1;
+      if (!warp_wait(bar + 8 * (B_LFULL + ls), (u >> 1) & 1, abort_flag, &wsh->error) ||
+          !warp_wait(bar + 8 * B_OFULL, u & 1, abort_flag, &wsh->error))
+        break;
       tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      __half* orow = p.o + (((size_t)b * p.n_q + q0 + r) * p.n_heads + h) * PHD;
+      const float lt = lsum[ls * BM + r];
+      mbar_arrive(bar + 8 * (B_LEMPTY + ls));
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      uint32_t packed[64];
 #pragma unroll
       for (int c = 0; c < 4; c++) {
         float ov[32];
-        tmem_ld32(tmem_o + lane_base + c * 32, ov);
+        tmem_ld32(tmem + TMEM_O + lane_base + c * 32, ov);
         tmem_ld_wait();
-        if (r < nq_valid) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 v;
-            __half2 h0 = __floats2half2_rn(ov[i] * inv, ov[i + 1] * inv);
-            __half2 h1 = __floats2half2_rn(ov[i + 2] * inv, ov[i + 3] * inv);
-            __half2 h2 = __floats2half2_rn(ov[i + 4] * inv, ov[i + 5] * inv);
-            __half2 h3 = __floats2half2_rn(ov[i + 6] * inv, ov[i + 7] * inv);
-            v.x = *reinterpret_cast<uint32_t*>(&h0);
-            v.y = *reinterpret_cast<uint32_t*>(&h1);
-            v.z = *reinterpret_cast<uint32_t*>(&h2);
-            v.w = *reinterpret_cast<uint32_t*>(&h3);
-            *reinterpret_cast<uint4*>(orow + c * 32 + i) = v;
-          }
+        for (int i = 0; i < 32; i += 2) {
+          __half2 h2 = __floats2half2_rn(ov[i] * inv, ov[i + 1] * inv);
+          packed[c * 16 + i / 2] = *reinterpret_cast<uint32_t*>(&h2);
         }
+      }
+      tc_fence_before();
+      mbar_arrive(bar + 8 * B_OEMPTY);
+      if (r < t.nq) {
+        uint4* orow = reinterpret_cast<uint4*>(
+            p.o + (((size_t)t.b * p.n_q + t.q0 + r) * p.n_heads + t.h) * PHD);
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+          orow[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
+                               packed[4 * i + 3]);
       }
     }
   }
@@ -571,9 +752,12 @@ int nwd_attn_prefill(const uint16_t* q, const uint16_t* k_pool, const uint16_t* 
   p.q_tiles = (n_q + BM - 1) / BM;
   const float sc = scale != 0.f ? scale : 1.0f / sqrtf((float)head_dim);
   p.scale_log2 = sc * 1.4426950408889634f;
-  const uint64_t grid = (uint64_t)batch * n_heads * p.q_tiles;
-  if (grid > 0x7fffffffull) return fail(NWD_ERR_UNSUPPORTED, "%s: too many tiles", who);
-  prefill_kernel<<<(uint32_t)grid, PTHR, P_SMEM_BYTES, (cudaStream_t)stream>>>(tq, tk, tv, p);
+  const uint64_t tiles = (uint64_t)batch * n_heads * p.q_tiles;
+  if (tiles > 0x7fffffffull) return fail(NWD_ERR_UNSUPPORTED, "%s: too many tiles", who);
+  p.n_tiles = (uint32_t)tiles;
+  // persistent: one CTA per SM (shared memory and TMEM allow no second one)
+  const uint32_t grid = (uint32_t)std::min<uint64_t>(tiles, (uint64_t)di.sm_count);
+  prefill_kernel<<<grid, PTHR, P_SMEM_BYTES, (cudaStream_t)stream>>>(tq, tk, tv, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, who);
   return ok();

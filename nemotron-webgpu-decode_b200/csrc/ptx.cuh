@@ -46,6 +46,18 @@ static __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t pari
       : "memory");
   return ok != 0;
 }
+// Non-blocking test of a phase (never suspends the thread).
+static __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait.  Returns false if the CTA is aborting (another thread gave
 // up) or this wait ran past its limits (then it raises the abort itself).
 static __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int32_t* abort,

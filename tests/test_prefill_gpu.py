@@ -64,3 +64,25 @@ def test_prefill_workspace_clean(ops):
                           workspace=ws)
     assert ws.check() == 0
     assert torch.isfinite(o.float()).all()
+
+
+@pytest.mark.parametrize("n_q,start_pos", [(200, 0), (256, 300), (77, 1000)])
+def test_prefill_ignores_rows_past_chunk(ops, oracle, n_q, start_pos):
+    """Cache rows past the chunk's end hold NaN (an unwritten pool): the key
+    block that straddles the end must not let them into the output."""
+    nh, nkv, hd, extra = 8, 2, 128, 200
+    rows = start_pos + n_q + extra
+    kp = oracle.normal_f16(rows * nkv * hd, 11).reshape(rows, nkv, hd)
+    vp = oracle.normal_f16(rows * nkv * hd, 12).reshape(rows, nkv, hd)
+    q = oracle.normal_f16(n_q * nh * hd, 13).reshape(1, n_q, nh, hd)
+    nan = np.uint16(0x7E00)
+    kd, vd = kp.copy(), vp.copy()
+    kd[start_pos + n_q:] = nan
+    vd[start_pos + n_q:] = nan
+    ro = torch.zeros(1, dtype=torch.int64, device="cuda")
+    o = torch.empty((1, n_q, nh, hd), dtype=torch.float16, device="cuda")
+    ops.attention_prefill(to_dev(q), to_dev(kd), to_dev(vd), ro, o, start_pos, nh, nkv, hd)
+    got = vals(o)
+    assert np.isfinite(got).all()
+    ref = oracle.attention_prefill(q, kp, vp, np.zeros(1, np.int64), n_q, start_pos, nh, nkv, hd)
+    assert_attn_close(got, ref, f"n_q={n_q} start={start_pos} NaN past the chunk")
