@@ -199,6 +199,16 @@ int nwd_attn_decode_partial(const uint16_t* q, const uint16_t* k_pool, const uin
 int nwd_attn_merge(const float* part_o, const float* part_ml, uint16_t* o, uint32_t shards,
                    uint32_t batch, uint32_t n_heads, uint32_t head_dim, void* stream);
 
+/* The same merge over packed partials: shard s occupies
+ * packed[s * R * (head_dim + 2) ...], R = batch * n_heads, holding its o
+ * ([R][head_dim], as part_o) followed by its (m, l) pairs ([R][2], as
+ * part_ml).  A rank that points nwd_attn_decode_partial's part_o / part_ml at
+ * the two halves of one buffer can exchange its partials with a single
+ * all-gather and merge the gathered [shards][...] buffer here.  At most 4096
+ * shards.  No counterpart in the reference (it has no multi-device code). */
+int nwd_attn_merge_packed(const float* packed, uint16_t* o, uint32_t shards, uint32_t batch,
+                          uint32_t n_heads, uint32_t head_dim, void* stream);
+
 /* ------------------------------------------------------------------ */
 /* Prompt chunks (causal prefill)                                      */
 /* ------------------------------------------------------------------ */

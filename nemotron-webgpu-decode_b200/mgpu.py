@@ -5,10 +5,10 @@ Each sequence's KV rows are split into contiguous shards, shard r on rank r
 
 1. on every rank, the shard partial (m, l, o) of every (sequence, query head)
    over the rank's rows — ``nwd_attn_decode_partial``;
-2. one all-gather of the partials (B*Hq*(128 + 2) floats per rank, 66.5 KB for
-   4 sequences x 32 heads) over NVLink;
+2. one all-gather of the partials, packed in one buffer (B*Hq*(128 + 2) floats
+   per rank, 66.5 KB for 4 sequences x 32 heads) over NVLink;
 3. the log-sum-exp merge in rank order (= row order, deterministic) —
-   ``nwd_attn_merge`` — which every rank computes, so every rank holds O.
+   ``nwd_attn_merge_packed`` — which every rank computes, so every rank holds O.
 
 The exchange is small next to the KV stream (17 GB per step for 4 x 1M rows),
 so the step scales with the shard size.  The reference has no multi-device
@@ -51,6 +51,26 @@ def gather_partials(part_o: torch.Tensor, part_ml: torch.Tensor, group=None):
     return go, gml
 
 
+def gather_packed(packed: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather a rank's packed partials [n] into [world, n], rank order (one collective)."""
+    if not _dist_on():
+        return packed.unsqueeze(0)
+    world = dist.get_world_size(group)
+    g = packed.new_empty((world, packed.numel()))
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(g, packed, group=group)
+    else:
+        dist.all_gather(list(g.unbind(0)), packed, group=group)
+    return g
+
+
+def unpack_partials(g: torch.Tensor, batch: int, n_heads: int, head_dim: int):
+    """Views (part_o [world, B, Hq, hd], part_ml [world, B, Hq, 2]) of gathered packed partials."""
+    n = batch * n_heads * head_dim
+    return (g[:, :n].view(-1, batch, n_heads, head_dim),
+            g[:, n:].view(-1, batch, n_heads, 2))
+
+
 class ShardedDecode:
     """One rank's shard of a batch of long sequences, and the sharded step.
 
@@ -83,9 +103,13 @@ class ShardedDecode:
         shape = (self.pool_rows, n_kv_heads, head_dim)
         self.k_pool = torch.zeros(shape, dtype=torch.float16, device=self.device)
         self.v_pool = torch.zeros_like(self.k_pool)
-        self.part_o = torch.empty(self.B, n_heads, head_dim, dtype=torch.float32,
+        # o and (m, l) partials in one buffer, exchanged with one collective
+        n = self.B * n_heads * head_dim
+        self.packed = torch.empty(n + self.B * n_heads * 2, dtype=torch.float32,
                                   device=self.device)
-        self.part_ml = torch.empty(self.B, n_heads, 2, dtype=torch.float32, device=self.device)
+        self.part_o = self.packed[:n].view(self.B, n_heads, head_dim)
+        self.part_ml = self.packed[n:].view(self.B, n_heads, 2)
+        self._merge_packed = merge_fn is None
         if partial_fn is None or merge_fn is None:
             from . import ops
             self._ops = ops
@@ -123,5 +147,12 @@ class ShardedDecode:
             out = torch.empty(self.B, self.n_heads, self.head_dim, dtype=torch.float16,
                               device=self.device)
         part_o, part_ml = self.partial_fn(q)
-        go, gml = gather_partials(part_o, part_ml, self.group)
+        if part_o.data_ptr() != self.part_o.data_ptr():  # an injected partial_fn
+            self.part_o.copy_(part_o)
+        if part_ml.data_ptr() != self.part_ml.data_ptr():
+            self.part_ml.copy_(part_ml)
+        g = gather_packed(self.packed, self.group)
+        if self._merge_packed:
+            return self._ops.merge_packed(g, out)
+        go, gml = unpack_partials(g, self.B, self.n_heads, self.head_dim)
         return self.merge_fn(go, gml, out)

@@ -237,6 +237,25 @@ def merge(part_o, part_ml, o, stream=None) -> torch.Tensor:
     return o
 
 
+def packed_partials(batch: int, n_heads: int, head_dim: int = 128, device=None):
+    """One buffer of B*n_heads*(hd+2) f32 and its (part_o, part_ml) views, the layout
+    nwd_attn_merge_packed reads (o first, then the (m, l) pairs)."""
+    n = batch * n_heads * head_dim
+    buf = torch.empty(n + batch * n_heads * 2, dtype=torch.float32, device=device)
+    return buf, buf[:n].view(batch, n_heads, head_dim), buf[n:].view(batch, n_heads, 2)
+
+
+def merge_packed(packed, o, stream=None) -> torch.Tensor:
+    """LSE-merge gathered packed partials [shards, B*n_heads*(hd+2)] into o [B, n_heads, hd]."""
+    shards = packed.shape[0]
+    batch, n_heads, hd = o.shape[-3], o.shape[-2], o.shape[-1]
+    if packed.numel() != shards * batch * n_heads * (hd + 2):
+        raise ValueError("packed partials do not match o's shape")
+    call("nwd_attn_merge_packed", _ptr(packed, torch.float32, "packed"), _h(o, "o"), shards,
+         batch, n_heads, hd, _stream(stream))
+    return o
+
+
 class Scratch:
     """A zeroed 256-byte-aligned device header for calls that only need the
     error word (prefill, multi-row appends)."""

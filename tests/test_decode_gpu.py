@@ -237,6 +237,36 @@ def test_partial_and_merge(ops, oracle):
     assert_attn_close(vals(o), ref, "3-shard merge")
 
 
+@pytest.mark.parametrize("shards", [1, 3, 6])
+def test_merge_packed(ops, oracle, shards):
+    """Partials written straight into packed buffers (o, then (m, l)), one buffer per
+    shard as an all-gather would deliver them; merge_packed == merge, and == whole."""
+    nh, nkv, hd, L, B = 16, 4, 128, 9000, 2
+    q = oracle.normal_f16(B * nh * hd, 61)
+    k = oracle.normal_f16(B * L * nkv * hd, 62)
+    v = oracle.normal_f16(B * L * nkv * hd, 63)
+    dq, dk, dv = to_dev(q, (B, nh, hd)), to_dev(k, (B * L, nkv, hd)), to_dev(v, (B * L, nkv, hd))
+    cuts = [L * i // shards for i in range(shards + 1)]
+    bufs = []
+    for a, b in zip(cuts[:-1], cuts[1:]):
+        buf, po, pml = ops.packed_partials(B, nh, hd, device="cuda")
+        offs = torch.tensor([a, L + a], dtype=torch.int64, device="cuda")
+        lens = torch.tensor([b - a, b - a], dtype=torch.int32, device="cuda")
+        ops.attention_partial(dq, dk, dv, offs, lens, po, pml, nh, nkv, hd)
+        bufs.append(buf)
+    g = torch.stack(bufs)
+    o_packed = torch.empty(B, nh, hd, dtype=torch.float16, device="cuda")
+    ops.merge_packed(g, o_packed)
+    n = B * nh * hd
+    o_plain = torch.empty_like(o_packed)
+    ops.merge(g[:, :n].reshape(shards, B, nh, hd).contiguous(),
+              g[:, n:].reshape(shards, B, nh, 2).contiguous(), o_plain)
+    assert torch.equal(o_packed, o_plain)
+    ref = oracle.attention_batched(q, k, v, np.array([0, L], np.int64),
+                                   np.array([L, L], np.int32), nh, nkv, hd)
+    assert_attn_close(vals(o_packed), ref, f"{shards}-shard packed merge")
+
+
 def test_long_sequence_262k(ops, oracle):
     """A 262144-row sequence (1 GiB of K+V) against the oracle."""
     nh, nkv, hd, L = 32, 8, 128, 262144
