@@ -210,6 +210,42 @@ int nwd_attn_merge_packed(const float* packed, uint16_t* o, uint32_t shards, uin
                           uint32_t n_heads, uint32_t head_dim, void* stream);
 
 /* ------------------------------------------------------------------ */
+/* The q4 projections either side of the path                          */
+/* ------------------------------------------------------------------ */
+
+/* kernels/matmul_nbits_sg.wgsl (the engine's decode GEMV, picked by
+ * engine/runtime.js:221-233, params uniform runtime.js:212-218): Y[N] f32 from
+ * A[K] f32 and 4-bit weights in the MatMulNBits layout the engine loads:
+ * b = [N][n_blocks][4] u32 (32 values per block, element j of a word in bits
+ * [4j, 4j+4), 16-byte aligned), scales = [N][n_blocks] f32, zp = 4-bit zero
+ * points packed 8 per u32, nibble n*n_blocks + blk.  Element value
+ * (q - zero) * scale; K must be 32 * n_blocks (at most 32768).  epilogue:
+ * 0 = store, 1 = relu2 (matmul_nbits_sg.wgsl:76-79, the MLP up projection),
+ * 2 = Y[n] += result (the residual add of kernels/add.wgsl fused, as
+ * runtime.js:392-393 applies it after o_proj). */
+int nwd_q4_gemv(const float* a, const uint32_t* b, const float* scales, const uint32_t* zp,
+                float* y, uint32_t K, uint32_t N, uint32_t n_blocks, uint32_t epilogue,
+                void* stream);
+
+/* The same GEMV with A in fp16, for o_proj fed by the fp16 attention output
+ * (the reference's attention output buffer is f32: runtime.js:334). */
+int nwd_q4_gemv_f16a(const uint16_t* a, const uint32_t* b, const float* scales,
+                     const uint32_t* zp, float* y, uint32_t K, uint32_t N, uint32_t n_blocks,
+                     uint32_t epilogue, void* stream);
+
+/* An attention layer's three projections in one launch, with the token's
+ * k / v written straight into the caches: runtime.js:389-391's q, k and v
+ * GEMVs (:321-329) followed by kv_append of k and of v.  h = the normalised
+ * hidden state [K] f32; q_out [n_heads * head_dim] fp16; the k and v results
+ * go to cache row `seq` ([cap][n_kv_heads][head_dim] fp16).  seq >= cap fails
+ * with "seq N exceeds maxSeq M" (runtime.js:448) before any launch. */
+int nwd_q4_qkv_append(const float* h, const uint32_t* bq, const float* sq, const uint32_t* zq,
+                      const uint32_t* bk, const float* sk, const uint32_t* zk, const uint32_t* bv,
+                      const float* sv, const uint32_t* zv, uint16_t* q_out, uint16_t* k_cache,
+                      uint16_t* v_cache, uint32_t seq, uint32_t cap, uint32_t K,
+                      uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, void* stream);
+
+/* ------------------------------------------------------------------ */
 /* Prompt chunks (causal prefill)                                      */
 /* ------------------------------------------------------------------ */
 

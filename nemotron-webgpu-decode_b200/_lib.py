@@ -69,6 +69,10 @@ SIGNATURES = {
                                                _u32, _f32, _P, _sz, _P]),
     "nwd_attn_merge": (ctypes.c_int, [_P, _P, _P, _u32, _u32, _u32, _u32, _P]),
     "nwd_attn_merge_packed": (ctypes.c_int, [_P, _P, _u32, _u32, _u32, _u32, _P]),
+    "nwd_q4_gemv": (ctypes.c_int, [_P, _P, _P, _P, _P, _u32, _u32, _u32, _u32, _P]),
+    "nwd_q4_gemv_f16a": (ctypes.c_int, [_P, _P, _P, _P, _P, _u32, _u32, _u32, _u32, _P]),
+    "nwd_q4_qkv_append": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                         _u32, _u32, _u32, _u32, _u32, _u32, _P]),
     "nwd_fill_normal_f16": (ctypes.c_int, [_P, _u64, _u64, _u64, _P]),
     "nwd_kv_append_rows": (ctypes.c_int, [_P, _P, _P, _P, _u64, _P, _u32, _u32, _u32, _u32, _u32,
                                           _P, _sz, _P]),

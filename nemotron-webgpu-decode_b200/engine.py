@@ -54,11 +54,84 @@ class DecodeAttention:
         self.seq += 1
         return out
 
+    def prefill(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """A prompt chunk of n tokens in two launches instead of n steps.
+
+        runtime.js:640-646 feeds a prompt one decode step per token; token i of
+        this chunk sees exactly the rows those steps would give it (0 .. seq + i).
+        q [n, heads, hd], k / v [n, kv_heads, hd] -> o [n, heads, hd]; the chunk's
+        k / v rows land at rows seq .. seq + n - 1 (the kv_append path for many
+        rows) and seq advances by n.  A chunk that would run past maxSeq is
+        refused before any launch, with the error the first step past it throws.
+        """
+        n = int(q.shape[0])
+        if self.seq + n > self.max_seq:
+            raise NwdError(NWD_ERR_RANGE, f"seq {self.max_seq} exceeds maxSeq {self.max_seq}")
+        if out is None:
+            out = torch.empty(n, self.heads, self.head_dim, dtype=torch.float16,
+                              device=self.device)
+        if n == 0:
+            return out
+        if not hasattr(self, "_row0"):
+            self._row0 = torch.zeros(1, dtype=torch.int64, device=self.device)
+        kv_shape = (1, n, self.kv_heads, self.head_dim)
+        ops.kv_append_rows(k.reshape(kv_shape), v.reshape(kv_shape), self.k_cache, self.v_cache,
+                           self._row0, self.seq, workspace=self.workspace, stream=stream)
+        ops.attention_prefill(q.reshape(1, n, self.heads, self.head_dim), self.k_cache,
+                              self.v_cache, self._row0, out.view(1, n, self.heads, self.head_dim),
+                              self.seq, self.heads, self.kv_heads, self.head_dim,
+                              scale=self.scale, workspace=self.workspace, stream=stream)
+        self.seq += n
+        return out
+
     def reset(self) -> None:
         """runtime.js:615-633: seq = 0 and the caches wiped."""
         self.seq = 0
         self.k_cache.zero_()
         self.v_cache.zero_()
+
+
+class AttentionLayer:
+    """One attention layer of the engine with the projections either side of the
+    path (runtime.js:321-335 builds it, :385-394 dispatches it): the q / k / v q4
+    GEMVs of the normalised hidden state, kv_append of k and v, attention, the
+    o_proj q4 GEMV and the residual add into the hidden state.  Here: one launch
+    for q/k/v with k/v written straight into the caches, one for attention, one for
+    o_proj with the residual add fused.  Weights stay in the MatMulNBits layout
+    (:class:`ops.Q4Weights`)."""
+
+    def __init__(self, wq: ops.Q4Weights, wk: ops.Q4Weights, wv: ops.Q4Weights,
+                 wo: ops.Q4Weights, heads: int = NANO4B_HEADS, kv_heads: int = NANO4B_KV_HEADS,
+                 head_dim: int = NANO4B_HEAD_DIM, max_seq: int = NANO4B_MAX_SEQ, device="cuda",
+                 scale: float = 0.0):
+        self.attn = DecodeAttention(heads, kv_heads, head_dim, max_seq, device, scale)
+        self.wq, self.wk, self.wv, self.wo = wq, wk, wv, wo
+        dev = self.attn.device
+        self.q = torch.empty(heads, head_dim, dtype=torch.float16, device=dev)
+        self.o = torch.empty(heads, head_dim, dtype=torch.float16, device=dev)
+
+    @property
+    def seq(self) -> int:
+        return self.attn.seq
+
+    def step(self, h_norm: torch.Tensor, h: torch.Tensor, stream=None) -> torch.Tensor:
+        """h += o_proj(attention(q, K, V)) for this token; h_norm [hidden] f32 is the
+        layer's normalised input, h [hidden] f32 the residual stream (updated in place)."""
+        a = self.attn
+        if a.seq >= a.max_seq:
+            raise NwdError(NWD_ERR_RANGE, f"seq {a.seq} exceeds maxSeq {a.max_seq}")
+        ops.q4_qkv_append(h_norm, self.wq, self.wk, self.wv, self.q, a.k_cache, a.v_cache,
+                          a.seq, stream=stream)
+        ops.attention(self.q, a.k_cache, a.v_cache, self.o,
+                      ops.AttnParams(a.heads, a.kv_heads, a.head_dim, a.seq + 1),
+                      scale=a.scale, workspace=a.workspace, stream=stream)
+        ops.q4_gemv(self.o.view(-1), self.wo, y=h, epilogue=2, stream=stream)
+        a.seq += 1
+        return h
+
+    def reset(self) -> None:
+        self.attn.reset()
 
 
 class BatchedDecodeAttention:

@@ -310,6 +310,67 @@ def attention_prefill(q, k_pool, v_pool, row_offset, o, start_pos: int, n_heads:
     return o
 
 
+@dataclass
+class Q4Weights:
+    """One q4 matrix in the reference's MatMulNBits layout (what the engine loads):
+    b [N, n_blocks, 4] uint32 (int32 storage is accepted), scales [N, n_blocks] f32,
+    zp [ceil(N*n_blocks/8)] uint32 (4-bit zero points, 8 per word)."""
+    b: torch.Tensor
+    scales: torch.Tensor
+    zp: torch.Tensor
+
+    @property
+    def n(self) -> int:
+        return int(self.scales.shape[0])
+
+    @property
+    def n_blocks(self) -> int:
+        return int(self.scales.shape[1])
+
+    def ptrs(self):
+        for t, name in ((self.b, "b"), (self.zp, "zp")):
+            if t.dtype not in (torch.int32, torch.uint32):
+                raise TypeError(f"q4 {name} must be 32-bit words, got {t.dtype}")
+            if not (t.is_cuda and t.is_contiguous()):
+                raise ValueError(f"q4 {name} must be a contiguous CUDA tensor")
+        return self.b.data_ptr(), _ptr(self.scales, torch.float32, "scales"), self.zp.data_ptr()
+
+
+def q4_gemv(a: torch.Tensor, w: Q4Weights, y: torch.Tensor | None = None, epilogue: int = 0,
+            stream=None) -> torch.Tensor:
+    """kernels/matmul_nbits_sg.wgsl: y [N] f32 from a [K] (f32, or fp16 for o_proj).
+    epilogue 0 = store, 1 = relu2, 2 = y += result (residual add)."""
+    if y is None:
+        y = torch.zeros(w.n, dtype=torch.float32, device=a.device)
+    K = a.numel()
+    bp, sp, zp = w.ptrs()
+    if a.dtype == torch.float16:
+        call("nwd_q4_gemv_f16a", _h(a, "a"), bp, sp, zp, _ptr(y, torch.float32, "y"), K, w.n,
+             w.n_blocks, int(epilogue), _stream(stream))
+    else:
+        call("nwd_q4_gemv", _ptr(a, torch.float32, "a"), bp, sp, zp, _ptr(y, torch.float32, "y"),
+             K, w.n, w.n_blocks, int(epilogue), _stream(stream))
+    return y
+
+
+def q4_qkv_append(h: torch.Tensor, wq: Q4Weights, wk: Q4Weights, wv: Q4Weights,
+                  q_out: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, seq: int,
+                  stream=None) -> torch.Tensor:
+    """The layer's q / k / v projections in one launch; k and v land in cache row `seq`
+    ([cap, n_kv, hd] fp16), q in q_out [n_heads, hd] fp16 (runtime.js:321-329, :389-391)."""
+    cap, n_kv, hd = k_cache.shape
+    n_heads = q_out.numel() // hd
+    if wq.n != n_heads * hd or wk.n != n_kv * hd or wv.n != n_kv * hd:
+        raise ValueError("q/k/v weight columns do not match the output shapes")
+    qb, qs, qz = wq.ptrs()
+    kb, ks, kz = wk.ptrs()
+    vb, vs, vz = wv.ptrs()
+    call("nwd_q4_qkv_append", _ptr(h, torch.float32, "h"), qb, qs, qz, kb, ks, kz, vb, vs, vz,
+         _h(q_out, "q_out"), _h(k_cache, "k_cache"), _h(v_cache, "v_cache"), int(seq), cap,
+         h.numel(), n_heads, n_kv, hd, _stream(stream))
+    return q_out
+
+
 def fill_normal(t: torch.Tensor, seed: int, offset: int = 0, stream=None) -> torch.Tensor:
     """Fill an fp16 tensor with the deterministic N(0,1) stream (bit-identical to the CPU
     generator used by the tests)."""
@@ -321,5 +382,6 @@ __all__ = [
     "KvParams", "AttnParams", "Workspace", "NwdError", "kv_append", "kv_append_kv",
     "kv_append_batched", "attention", "kv_append_attention", "attention_batched",
     "kv_append_attention_batched", "attention_partial", "merge", "fill_normal", "Scratch",
-    "kv_append_rows", "attention_prefill",
+    "kv_append_rows", "attention_prefill", "packed_partials", "merge_packed", "Q4Weights",
+    "q4_gemv", "q4_qkv_append",
 ]

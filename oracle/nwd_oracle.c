@@ -15,6 +15,9 @@
  *     (kernels/sparse_attn.wgsl:29).
  *   - engine/runtime.js:447-467 step sequencing (append row seq, attend
  *     seq + 1 rows) is exercised by the callers in tests/.
+ *   - kernels/matmul_nbits_sg.wgsl:32-137 (+ kernels/add.wgsl:15-16) ->
+ *     oracle_q4_gemv_f32: the q4 GEMV of the projections either side of
+ *     the path (q/k/v before it, o_proj + residual after it).
  *
  * Parity status: UNPINNED.  The reference ships no tests, golden vectors or
  * CPU implementation of this path, and its WGSL needs a WebGPU device
@@ -418,4 +421,107 @@ void oracle_set_num_threads(int n) {
 #else
     (void)n;
 #endif
+}
+
+/* ---------------- q4 GEMV: the projections either side of the path ---------------- */
+
+/* kernels/matmul_nbits_sg.wgsl:32-137, the GEMV the engine runs for an
+ * attention layer's q/k/v projections (runtime.js:321-329) and its o_proj
+ * (:330, followed by the residual add of kernels/add.wgsl, runtime.js:392-393).
+ * Weights of column n: n_blocks blocks of 32 four-bit values, 16 bytes (four
+ * u32 words) per block; element j of a word is bits [4j, 4j+4) (a byte holds
+ * elements 2b in its low nibble and 2b+1 in its high nibble, :38-41); one f32
+ * scale per block ([N][n_blocks]); one 4-bit zero point per block, packed 8 per
+ * u32, nibble n*n_blocks + blk, low nibble first (:28-31).  Element value
+ * (q - zero) * scale.  The reference sums a block word by word, each word as
+ * dot(a0, d0) + dot(a1, d1) (:33-64, dot taken left to right here); thread t of
+ * its 256 adds blocks t, t+256, ... in order (:101-128); each subgroup of 32
+ * reduces by xor shuffles 1, 2, .., 16 (:66-74: a pairwise tree, lane 0 kept)
+ * and the 8 subgroup sums are added in order (:129-135).  epilogue 1 = relu2
+ * (:76-79); epilogue 2 = the engine's residual add, Y[n] = Y[n] + result
+ * (kernels/add.wgsl:15-16). */
+static float q4_word_dot(uint32_t p, float s, float z, const float* a) {
+    float d[8];
+    for (int j = 0; j < 8; j++) d[j] = ((float)((p >> (4 * j)) & 15u) - z) * s;
+    const float d0 = ((a[0] * d[0] + a[1] * d[1]) + a[2] * d[2]) + a[3] * d[3];
+    const float d1 = ((a[4] * d[4] + a[5] * d[5]) + a[6] * d[6]) + a[7] * d[7];
+    return d0 + d1;
+}
+
+static float q4_zero(const uint32_t* zp, uint64_t nib) {
+    return (float)((zp[nib / 8u] >> ((nib % 8u) * 4u)) & 15u);
+}
+
+void oracle_q4_gemv_f32(const float* A, const uint32_t* B, const float* scales,
+                        const uint32_t* zp, float* Y, uint32_t N, uint32_t n_blocks,
+                        uint32_t epilogue) {
+#pragma omp parallel for schedule(static)
+    for (int64_t n = 0; n < (int64_t)N; n++) {
+        float lane[256];
+        for (int t = 0; t < 256; t++) lane[t] = 0.0f;
+        for (uint32_t blk = 0; blk < n_blocks; blk++) {
+            const uint64_t i = (uint64_t)n * n_blocks + blk;
+            float acc = 0.0f;
+            for (int w = 0; w < 4; w++)
+                acc += q4_word_dot(B[4 * i + w], scales[i], q4_zero(zp, i), A + 32ull * blk + 8 * w);
+            lane[blk % 256u] += acc;
+        }
+        float tot = 0.0f;
+        for (int sg = 0; sg < 8; sg++) {
+            float v[32];
+            memcpy(v, lane + 32 * sg, sizeof v);
+            for (int step = 1; step < 32; step <<= 1)
+                for (int i = 0; i < 32; i += 2 * step) v[i] = v[i] + v[i + step];
+            tot += v[0];
+        }
+        if (epilogue == 1) {
+            const float r = tot > 0.0f ? tot : 0.0f;
+            tot = r * r;
+        } else if (epilogue == 2) {
+            tot = Y[n] + tot;
+        }
+        Y[n] = tot;
+    }
+}
+
+/* The same GEMV in float64 (any order), to size the f32 rounding. */
+void oracle_q4_gemv_f64(const float* A, const uint32_t* B, const float* scales,
+                        const uint32_t* zp, double* Y, uint32_t N, uint32_t n_blocks) {
+#pragma omp parallel for schedule(static)
+    for (int64_t n = 0; n < (int64_t)N; n++) {
+        double tot = 0.0;
+        for (uint32_t blk = 0; blk < n_blocks; blk++) {
+            const uint64_t i = (uint64_t)n * n_blocks + blk;
+            const double s = scales[i], z = q4_zero(zp, i);
+            for (int j = 0; j < 32; j++) {
+                const uint32_t q = (B[4 * i + j / 8] >> (4 * (j % 8))) & 15u;
+                tot += (double)A[32ull * blk + j] * (((double)q - z) * s);
+            }
+        }
+        Y[n] = tot;
+    }
+}
+
+/* Deterministic synthetic q4 weights (not part of the reference): packed words
+ * are raw splitmix64 bits (uniform nibbles), zero points likewise, scales
+ * 2^-9 + u * 2^-7 with u a 16-bit uniform (exact in f32). */
+void oracle_fill_q4(uint32_t* B, float* scales, uint32_t* zp, uint32_t N, uint32_t n_blocks,
+                    uint64_t seed) {
+    const uint64_t blocks = (uint64_t)N * n_blocks;
+    const uint64_t mix = splitmix64(seed);
+#pragma omp parallel for schedule(static) if (blocks > 4096)
+    for (int64_t i = 0; i < (int64_t)blocks; i++) {
+        const uint64_t h0 = splitmix64(mix + 4ull * (uint64_t)i);
+        const uint64_t h1 = splitmix64(mix + 4ull * (uint64_t)i + 1);
+        const uint64_t h2 = splitmix64(mix + 4ull * (uint64_t)i + 2);
+        B[4 * i + 0] = (uint32_t)h0;
+        B[4 * i + 1] = (uint32_t)(h0 >> 32);
+        B[4 * i + 2] = (uint32_t)h1;
+        B[4 * i + 3] = (uint32_t)(h1 >> 32);
+        scales[i] = 0.001953125f + (float)(h2 & 0xffffu) * (0.0078125f / 65536.0f);
+    }
+    const uint64_t words = (blocks + 7) / 8;
+#pragma omp parallel for schedule(static) if (words > 4096)
+    for (int64_t w = 0; w < (int64_t)words; w++)
+        zp[w] = (uint32_t)splitmix64(mix ^ 0x5a5a5a5a5a5a5a5aull ^ (uint64_t)w);
 }

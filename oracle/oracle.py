@@ -4,9 +4,10 @@ TEST INFRASTRUCTURE ONLY: imported by ``tests/``, ``__graft_entry__.smoke()``
 and the CPU-baseline legs of ``bench.py``, as the checker or the timed CPU
 baseline.  The product path (``nemotron-webgpu-decode_b200``) never imports it.
 
-The C file restates ``kernels/sparse_attn.wgsl:32-113`` and
-``kernels/kv_append.wgsl:13-18`` of the reference; parity is unpinned (the
-reference has no tests or golden vectors, and its WGSL cannot run here).
+The C file restates ``kernels/sparse_attn.wgsl:32-113``,
+``kernels/kv_append.wgsl:13-18`` and the q4 GEMV ``kernels/matmul_nbits_sg.wgsl``
+(+ ``kernels/add.wgsl``) of the reference; parity is unpinned (the reference has
+no tests or golden vectors, and its WGSL cannot run here).
 """
 from __future__ import annotations
 
@@ -26,6 +27,7 @@ _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _f64p = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")
 _i64p = np.ctypeslib.ndpointer(np.int64, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
 _u32 = ctypes.c_uint32
 _u64 = ctypes.c_uint64
 
@@ -64,6 +66,9 @@ def lib():
         L.oracle_attn_merge.argtypes = [_f32p, _f32p, _f32p, _u32, _u32, _u32]
         L.oracle_attn_prefill_f32.argtypes = [_u16p, _u16p, _u16p, _i64p, _f32p, _u32, _u32, _u32,
                                               _u32, _u32, _u32, ctypes.c_float]
+        L.oracle_q4_gemv_f32.argtypes = [_f32p, _u32p, _f32p, _u32p, _f32p, _u32, _u32, _u32]
+        L.oracle_q4_gemv_f64.argtypes = [_f32p, _u32p, _f32p, _u32p, _f64p, _u32, _u32]
+        L.oracle_fill_q4.argtypes = [_u32p, _f32p, _u32p, _u32, _u32, _u64]
         L.oracle_num_threads.restype = ctypes.c_int
         L.oracle_set_num_threads.argtypes = [ctypes.c_int]
         _lib = L
@@ -175,6 +180,39 @@ def attention_prefill(q, k_pool, v_pool, row_offset, n_q: int, start_pos: int, n
     lib().oracle_attn_prefill_f32(_u16(q).reshape(-1), _u16(k_pool).reshape(-1),
                                   _u16(v_pool).reshape(-1), row_offset, out.reshape(-1), batch,
                                   n_q, start_pos, n_heads, n_kv_heads, head_dim, float(scale))
+    return out
+
+
+def q4_weights(n: int, n_blocks: int, seed: int):
+    """Deterministic synthetic q4 weights: packed [N, n_blocks, 4] u32, scales [N, n_blocks]
+    f32, zero points [ceil(N*n_blocks/8)] u32 (the MatMulNBits layout)."""
+    B = np.empty((n, n_blocks, 4), np.uint32)
+    scales = np.empty((n, n_blocks), np.float32)
+    zp = np.empty(((n * n_blocks + 7) // 8,), np.uint32)
+    lib().oracle_fill_q4(B.reshape(-1), scales.reshape(-1), zp, n, n_blocks, int(seed))
+    return B, scales, zp
+
+
+def q4_gemv(a, B, scales, zp, epilogue: int = 0, y=None) -> np.ndarray:
+    """kernels/matmul_nbits_sg.wgsl: Y [N] f32 from A [K] f32 (epilogue 1 = relu2,
+    2 = Y += result, the engine's residual add)."""
+    n, n_blocks = scales.shape
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    assert a.size == 32 * n_blocks
+    out = np.zeros(n, np.float32) if y is None else np.array(y, dtype=np.float32, copy=True)
+    lib().oracle_q4_gemv_f32(a, np.ascontiguousarray(B, np.uint32).reshape(-1),
+                             np.ascontiguousarray(scales, np.float32).reshape(-1),
+                             np.ascontiguousarray(zp, np.uint32), out, n, n_blocks, int(epilogue))
+    return out
+
+
+def q4_gemv_f64(a, B, scales, zp) -> np.ndarray:
+    n, n_blocks = scales.shape
+    out = np.empty(n, np.float64)
+    lib().oracle_q4_gemv_f64(np.ascontiguousarray(a, dtype=np.float32),
+                             np.ascontiguousarray(B, np.uint32).reshape(-1),
+                             np.ascontiguousarray(scales, np.float32).reshape(-1),
+                             np.ascontiguousarray(zp, np.uint32), out, n, n_blocks)
     return out
 
 

@@ -158,6 +158,48 @@ def test_engine_trace_config1(engine_mod, oracle):
     assert layer.workspace.check() == 0
 
 
+def test_engine_prompt_chunk_then_steps(engine_mod, oracle):
+    """BASELINE config 1 with the 24-token prompt as one chunk (DecodeAttention.prefill,
+    the tcgen05 kernel) instead of 24 steps, then 127 decode steps: every output matches
+    the reference's token-by-token order (runtime.js:640-646)."""
+    nh, nkv, hd, cap, n_prompt = 40, 8, 128, 256, 24
+    layer = engine_mod.DecodeAttention(nh, nkv, hd, cap)
+    kc = np.zeros((cap, nkv, hd), np.uint16)
+    vc = np.zeros((cap, nkv, hd), np.uint16)
+    qs = [oracle.normal_f16(nh * hd, 1, t * nh * hd) for t in range(24 + 127)]
+    ks = [oracle.normal_f16(nkv * hd, 2, t * nkv * hd) for t in range(24 + 127)]
+    vs = [oracle.normal_f16(nkv * hd, 3, t * nkv * hd) for t in range(24 + 127)]
+    out = layer.prefill(to_dev(np.stack(qs[:n_prompt]), (n_prompt, nh, hd)),
+                        to_dev(np.stack(ks[:n_prompt]), (n_prompt, nkv, hd)),
+                        to_dev(np.stack(vs[:n_prompt]), (n_prompt, nkv, hd)))
+    assert layer.seq == n_prompt
+    got = vals(out)
+    for t in range(n_prompt):
+        oracle.kv_append(ks[t], kc, t, nkv, hd)
+        oracle.kv_append(vs[t], vc, t, nkv, hd)
+        ref = oracle.attention(qs[t], kc, vc, nh, nkv, hd, t + 1)
+        assert_attn_close(got[t], ref, f"prompt token {t}")
+    for t in range(n_prompt, 24 + 127):
+        out = layer.step(to_dev(qs[t], (nh, hd)), to_dev(ks[t], (nkv, hd)),
+                         to_dev(vs[t], (nkv, hd)))
+        oracle.kv_append(ks[t], kc, t, nkv, hd)
+        oracle.kv_append(vs[t], vc, t, nkv, hd)
+        assert_attn_close(vals(out), oracle.attention(qs[t], kc, vc, nh, nkv, hd, t + 1),
+                          f"step {t}")
+    assert np.array_equal(bits(layer.k_cache), kc) and np.array_equal(bits(layer.v_cache), vc)
+    assert layer.workspace.check() == 0
+
+
+def test_engine_prompt_chunk_past_max_seq(engine_mod, ops):
+    layer = engine_mod.DecodeAttention(32, 8, 128, max_seq=16)
+    q = torch.randn(10, 32, 128, device="cuda").half()
+    kv = torch.randn(10, 8, 128, device="cuda").half()
+    layer.prefill(q, kv, kv)
+    with pytest.raises(ops.NwdError, match="seq 16 exceeds maxSeq 16"):
+        layer.prefill(q, kv, kv)
+    assert layer.seq == 10
+
+
 def test_engine_max_seq_error(engine_mod, ops):
     layer = engine_mod.DecodeAttention(32, 8, 128, max_seq=2)
     q = torch.randn(32, 128, device="cuda").half()
