@@ -13,7 +13,12 @@ config 3's lengths however many steps run).  Sequences shard across GPUs with
 no communication; each GPU runs its own 256-sequence batch (weak scaling).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl nwd|reference]
-                  [--config 3|1|2] [--scaling weak|strong]
+                  [--config 3|1|2|4|5|6] [--scaling weak|strong]
+
+Other configs: 1 engine trace and 2 length sweep (single sequence, CUDA-graph
+replay), 4 chunked causal prefill (tcgen05), 5 long-context split-KV sharded
+over the GPUs (NCCL all-gather + merge), 6 the model's 4 attention layers with
+their q4 projections (q/k/v + append, attention, o_proj + residual).
 
 ``--impl reference`` times the reference's algorithm on the host CPU: the
 reference is WGSL for a browser WebGPU device, which this machine cannot run,
@@ -330,7 +335,8 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=30)
     ap.add_argument("--impl", choices=["nwd", "reference"], default="nwd")
-    ap.add_argument("--config", choices=["3", "1", "2", "4", "5"], default="3")
+    ap.add_argument("--config", choices=["3", "1", "2", "4", "5", "6"], default="3",
+                    help="BASELINE config (6 = the attention layers with their q4 projections)")
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
     ap.add_argument("--ramp-seconds", type=float, default=1.0)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -365,6 +371,8 @@ def main():
         return run_config5(args, ops, torch, dist, dev, rank, world)
     if args.config == "4":
         return run_config4(args, ops, torch, dist, dev, rank, world)
+    if args.config == "6":
+        return run_config6(args, ops, torch, dist, dev, rank, world)
     if args.config != "3":
         return run_small_configs(args, ops, torch, dev, rank, world)
 
@@ -704,6 +712,216 @@ def run_config4(args, ops, torch, dist, dev, rank, world):
         dist.barrier()
         dist.destroy_process_group()
     return 0 if err == 0 else 3
+
+
+HIDDEN6, HQ6 = 3136, 40          # engine/config.js: hidden, heads
+N_ATTN_LAYERS = 4                 # engine/config.js ATTN_LAYERS
+L6 = 150                          # rows already cached (config 1's trace end)
+WEIGHT_SETS = 3                   # rotating copies: 3 x 99 MB of q4 weights > L2
+
+
+def _q4_random(ops, torch, n, n_blocks, gen, dev):
+    """Synthetic q4 weights in the MatMulNBits layout (uniform nibbles, scales in
+    [2^-9, 2^-9 + 2^-7)), generated on the device."""
+    b = torch.randint(-2**31, 2**31 - 1, (n, n_blocks, 4), dtype=torch.int32, device=dev,
+                      generator=gen)
+    s = torch.rand(n, n_blocks, device=dev, generator=gen) * 0.0078125 + 0.001953125
+    z = torch.randint(-2**31, 2**31 - 1, ((n * n_blocks + 7) // 8,), dtype=torch.int32,
+                      device=dev, generator=gen)
+    return ops.Q4Weights(b, s, z)
+
+
+def run_config6(args, ops, torch, dist, dev, rank, world):
+    """Scope row (f): one decode token through the model's 4 attention layers with the
+    projections either side of the path, at the engine shape (hidden 3136, Hq 40,
+    Hkv 8, d 128, 150 cached rows): per layer the q/k/v q4 GEMVs with k/v appended
+    to the cache (one launch), attention, and the o_proj q4 GEMV with the residual
+    add (runtime.js:385-394).  Three rotating copies of the 4 layers' weights (296 MB)
+    keep every step's weights out of L2.  Each copy's 4 layers are captured once in
+    a CUDA graph (12 launches) and replayed.  Replicas only: a single sequence does
+    not shard."""
+    eng = importlib.import_module(PKG + ".engine")
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(6000 + rank)
+    nb_h, nb_o = HIDDEN6 // 32, HQ6 * HD // 32
+    sets = []
+    for _ in range(WEIGHT_SETS):
+        layers = []
+        for _ in range(N_ATTN_LAYERS):
+            layer = eng.AttentionLayer(_q4_random(ops, torch, HQ6 * HD, nb_h, gen, dev),
+                                       _q4_random(ops, torch, HKV * HD, nb_h, gen, dev),
+                                       _q4_random(ops, torch, HKV * HD, nb_h, gen, dev),
+                                       _q4_random(ops, torch, HIDDEN6, nb_o, gen, dev),
+                                       HQ6, HKV, HD, 256, dev)
+            ops.fill_normal(layer.attn.k_cache, 61 + rank)
+            ops.fill_normal(layer.attn.v_cache, 62 + rank)
+            layers.append(layer)
+        sets.append(layers)
+    h_norm = torch.randn(N_ATTN_LAYERS, HIDDEN6, device=dev, generator=gen)
+    h = torch.randn(HIDDEN6, device=dev, generator=gen)
+    weight_bytes = sum(w.b.numel() * 4 + w.scales.numel() * 4 + w.zp.numel() * 4
+                       for L in sets[0] for w in (L.wq, L.wk, L.wv, L.wo))
+    # algorithmic bytes per token: weights once, K/V rows attended, the new rows,
+    # q / o, the residual read + write and the activations
+    kv_bytes = N_ATTN_LAYERS * ((L6 + 1) * HKV * HD * 2 * 2 + 2 * HKV * HD * 2)
+    act_bytes = N_ATTN_LAYERS * (HIDDEN6 * 4 + 2 * HQ6 * HD * 2 * 2 + 2 * HIDDEN6 * 4)
+    step_bytes6 = weight_bytes + kv_bytes + act_bytes
+
+    stream = torch.cuda.Stream(device=dev)
+    graphs = []
+    with torch.cuda.stream(stream):
+        for layers in sets:  # eager once (sets the kernels' attributes), then capture
+            for i, L in enumerate(layers):
+                L.attn.seq = L6
+                L.step(h_norm[i], h)
+        torch.cuda.synchronize()
+        for layers in sets:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i, L in enumerate(layers):
+                    L.attn.seq = L6
+                    L.step(h_norm[i], h)
+            graphs.append(g)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    s = 0
+    for _ in range(args.warmup):
+        graphs[s % WEIGHT_SETS].replay()
+        s += 1
+    barrier()
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        graphs[s % WEIGHT_SETS].replay()
+        s += 1
+    e.record()
+    e.synchronize()
+    barrier()
+    ms = a.elapsed_time(e)
+    # the q/k/v launch alone (the largest kernel): one launch per layer of every weight
+    # copy (12, cold weights) captured in a graph, so the time is the GPU's alone
+    qkv_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(qkv_graph, stream=stream):
+            for layers in sets:
+                for L in layers:
+                    ops.q4_qkv_append(h_norm[0], L.wq, L.wk, L.wv, L.q, L.attn.k_cache,
+                                      L.attn.v_cache, L6, stream=stream)
+    torch.cuda.synchronize()
+    n_qkv = WEIGHT_SETS * N_ATTN_LAYERS
+    qkv_runs = []
+    for _ in range(5):
+        x, y = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        x.record()
+        qkv_graph.replay()
+        y.record()
+        y.synchronize()
+        qkv_runs.append(x.elapsed_time(y) / n_qkv)
+    qkv_ms = statistics.median(qkv_runs)
+    del qkv_graph
+    L0 = sets[0][0]
+    qkv_bytes = sum(w.b.numel() * 4 + w.scales.numel() * 4 + w.zp.numel() * 4
+                    for w in (L0.wq, L0.wk, L0.wv)) + HIDDEN6 * 4 + (HQ6 + 2 * HKV) * HD * 2
+    # e2e: the layers' inputs from pinned host memory and the residual stream back
+    e2e = None
+    if not args.no_e2e:
+        hn_h = h_norm.cpu().pin_memory()
+        h_h = torch.empty(HIDDEN6, dtype=torch.float32).pin_memory()
+        cur = torch.cuda.current_stream()
+        for _ in range(args.warmup):
+            h_norm.copy_(hn_h, non_blocking=True)
+            graphs[s % WEIGHT_SETS].replay()
+            h_h.copy_(h, non_blocking=True)
+            cur.synchronize()
+            s += 1
+        barrier()
+        a2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a2.record()
+        for _ in range(args.steps):
+            h_norm.copy_(hn_h, non_blocking=True)
+            graphs[s % WEIGHT_SETS].replay()
+            h_h.copy_(h, non_blocking=True)
+            cur.synchronize()
+            s += 1
+        e2.record()
+        e2.synchronize()
+        barrier()
+        e2e = a2.elapsed_time(e2)
+    ms_max, qkv_max, e2e_max = max_over_ranks([ms, qkv_ms, e2e or 0.0], dist, dev)
+    err = max(L.attn.workspace.check() for layers in sets for L in layers)
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_config6(args)
+    for g in graphs:
+        del g
+    graphs.clear()
+    if rank == 0:
+        peak, kind = peaks()
+        gbs = qkv_bytes / (qkv_ms * 1e-3) / 1e9
+        line = {
+            "metric": "attention-layer decode tokens/s (q/k/v q4 projections + append + "
+                      "attention + o_proj + residual, 4 layers)",
+            "value": world * args.steps / (ms_max * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (random q4 weights, N(0,1) activations and caches)",
+            "hbm_tbs": step_bytes6 / (ms_max / args.steps * 1e-3) / 1e12,
+            "config": {"workload": "row-f-attention-layers", "layers": N_ATTN_LAYERS,
+                       "hidden": HIDDEN6, "heads": HQ6, "kv_heads": HKV, "head_dim": HD,
+                       "cached_rows": L6, "weight_sets": WEIGHT_SETS,
+                       "weights_mb_per_step": weight_bytes / 1e6,
+                       "bytes_per_step": step_bytes6,
+                       "l2": "three rotating weight copies (296 MB) > L2",
+                       "launch": "CUDA graph per weight copy (12 launches)"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                         "frac": gbs / peak, "kernel": "q4_gemv_kernel (q/k/v + append)",
+                         "launch_ms": qkv_max, "bytes_per_launch": qkv_bytes,
+                         "traffic": None, "peak_source": f"{kind} (hbm_gbs)"},
+            "e2e": ({"value": world * args.steps / (e2e_max * 1e-3), "unit": "tokens/s",
+                     "h2d_bytes_per_step": N_ATTN_LAYERS * HIDDEN6 * 4,
+                     "d2h_bytes_per_step": HIDDEN6 * 4} if e2e is not None else None),
+            "cpu_baseline": cpu,
+            "gpu_launches": 12 * args.steps,
+            "device_error": err,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0 if err == 0 else 3
+
+
+def cpu_baseline_config6(args):
+    """The oracle (the reference's algorithm) for one attention layer with its
+    projections on the host cores, scaled to the 4 layers of a token."""
+    oracle = import_oracle()
+    nb_h, nb_o = HIDDEN6 // 32, HQ6 * HD // 32
+    wq = oracle.q4_weights(HQ6 * HD, nb_h, 1)
+    wk = oracle.q4_weights(HKV * HD, nb_h, 2)
+    wv = oracle.q4_weights(HKV * HD, nb_h, 3)
+    wo = oracle.q4_weights(HIDDEN6, nb_o, 4)
+    kc = oracle.normal_f16(256 * HKV * HD, 5).reshape(256, HKV, HD)
+    vc = oracle.normal_f16(256 * HKV * HD, 6).reshape(256, HKV, HD)
+    hn = oracle.f16_bits_to_f32(oracle.normal_f16(HIDDEN6, 7))
+    h = oracle.f16_bits_to_f32(oracle.normal_f16(HIDDEN6, 8))
+    reps, t0 = 0, time.perf_counter()
+    while reps < 3 or (time.perf_counter() - t0 < min(args.cpu_seconds, 5.0) and reps < 200):
+        q = oracle.f32_to_f16_bits(oracle.q4_gemv(hn, *wq))
+        oracle.kv_append(oracle.f32_to_f16_bits(oracle.q4_gemv(hn, *wk)), kc, L6, HKV, HD)
+        oracle.kv_append(oracle.f32_to_f16_bits(oracle.q4_gemv(hn, *wv)), vc, L6, HKV, HD)
+        o = oracle.attention(q, kc, vc, HQ6, HKV, HD, L6 + 1)
+        h = oracle.q4_gemv(o, *wo, epilogue=2, y=h)
+        reps += 1
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": 1.0 / (N_ATTN_LAYERS * dt), "unit": "tokens/s",
+            "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"{reps} single-layer steps (q/k/v, append, attention over {L6 + 1} rows, "
+                      f"o_proj + residual) on the oracle, scaled to {N_ATTN_LAYERS} layers"}
 
 
 def run_config5(args, ops, torch, dist, dev, rank, world):

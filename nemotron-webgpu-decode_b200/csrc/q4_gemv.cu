@@ -11,16 +11,19 @@
 // nibble n*n_blocks + blk).  Element value (q - zero) * scale.
 //
 // HBM-bound: a column's weights are read once (20.5 bytes per 32 elements).
-// A warp takes a group of 4 columns; the 4 lanes of a block each take one
-// 8-element word, so for each column the warp's 32 lanes read 8 consecutive
-// blocks = 128 contiguous bytes, and a lane keeps 4 block rows x 4 columns of
-// words in flight.  The lane's 8 activations are read once from shared memory
-// and used for all 4 columns.  A block's term is computed as
-//   scale * (sum_j a_j q_j - zero * sum_j a_j),
-// with the per-block sums of A formed once per CTA in shared memory, so an
-// element costs an integer extract, a float add and one FMA (no conversion
-// through the special-function unit).  f32 accumulation throughout; the lanes
-// are reduced with shuffles at the end of the column group.
+// A warp takes a group of 4 columns and walks them in rows of 32 blocks, one
+// block per lane: for each column a lane loads the block's 16 bytes, its scale
+// and its zero point, so a row is 512 contiguous bytes per column.  The loads
+// of the next two rows are in flight while a row is computed (software
+// pipelining) and the grid is sized to what stays resident.  The lane's 32
+// activations come from a shared-memory copy of A (float4s XOR-swizzled by
+// block, so the 32 lanes of a warp, reading 32 different blocks, hit distinct
+// banks) and serve all 4 columns.  A nibble q becomes the float 1 + q/16 with a
+// shift and one logic operation (q placed in the top mantissa bits), so
+//   sum_j a_j q_j = 16 * (sum_j a_j (1 + q_j/16) - sum_j a_j)
+// and a block contributes scale * (16 * sum_j a_j f_j - (16 + zero) * sum_j a_j):
+// three instructions per element, none through the special-function unit.
+// f32 accumulation; lanes are reduced with shuffles at the end of the group.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -31,9 +34,9 @@ namespace {
 
 constexpr int GEMV_THREADS = 128;      // 4 warps
 constexpr int CG = 4;                  // columns per warp
-constexpr int UNROLL = 4;              // block rows in flight per lane (x 8 block slots per warp)
-constexpr uint32_t MAX_BLOCKS = 1024;  // K <= 32768 (shared-memory copy of A and its block sums)
-constexpr size_t smem_bytes(uint32_t n_blocks) { return (size_t)n_blocks * 33 * sizeof(float); }
+constexpr int DEPTH = 2;               // rows of 32 blocks in flight ahead of the one computed
+constexpr uint32_t MAX_BLOCKS = 1024;  // K <= 32768 (shared-memory copy of A)
+constexpr size_t smem_bytes(uint32_t n_blocks) { return (size_t)n_blocks * 32 * sizeof(float); }
 
 enum OutMode : int {
   OUT_F32 = 0,  // Y[n] (epilogue 0), relu2 (1), Y[n] += (2)
@@ -59,50 +62,114 @@ struct GemvArgs {
   __half* v_row;
 };
 
-template <typename AT>
-__device__ __forceinline__ float a_at(const AT* a, uint32_t i);
-template <>
-__device__ __forceinline__ float a_at<float>(const float* a, uint32_t i) {
-  return __ldg(a + i);
-}
-template <>
-__device__ __forceinline__ float a_at<__half>(const __half* a, uint32_t i) {
-  return __half2float(a[i]);
+// 1 + q/16 for the 4-bit field q at bits [4E, 4E+4) of x: q moved to mantissa
+// bits 19-22 under the exponent of 1.0 (exact).  The move is an integer
+// multiply (by 2^s, or the high word of a multiply by 2^(32-s)), which runs on
+// the FMA pipe; only the mask-and-merge uses the integer ALU, which has half
+// the FMA pipe's throughput and would otherwise bound the kernel.
+template <int E>
+__device__ __forceinline__ float nib16(uint32_t x) {
+  constexpr int sh = 19 - 4 * E;
+  uint32_t t;
+  if (sh >= 0) {
+    asm("mul.lo.u32 %0, %1, %2;" : "=r"(t) : "r"(x), "n"(1u << (sh >= 0 ? sh : 0)));
+  } else {
+    asm("mul.hi.u32 %0, %1, %2;" : "=r"(t) : "r"(x), "n"(1u << (sh < 0 ? 32 + sh : 0)));
+  }
+  return __uint_as_float((t & 0x00780000u) | 0x3F800000u);
 }
 
-// float value of the 4-bit field at bit 4j of p: 2^23 + q as a float, minus 2^23 (exact)
-__device__ __forceinline__ float nib_f(uint32_t p, int j) {
-  return __uint_as_float(((p >> (4 * j)) & 15u) | 0x4B000000u) - 8388608.0f;
+// the 8 values of one weight word against 8 activations
+__device__ __forceinline__ float word_dot(uint32_t x, const float* a, float d) {
+  d = fmaf(a[0], nib16<0>(x), d);
+  d = fmaf(a[1], nib16<1>(x), d);
+  d = fmaf(a[2], nib16<2>(x), d);
+  d = fmaf(a[3], nib16<3>(x), d);
+  d = fmaf(a[4], nib16<4>(x), d);
+  d = fmaf(a[5], nib16<5>(x), d);
+  d = fmaf(a[6], nib16<6>(x), d);
+  d = fmaf(a[7], nib16<7>(x), d);
+  return d;
 }
+
+// shared-memory slot of float4 k (0..7) of block b
+__device__ __forceinline__ uint32_t a_slot(uint32_t b, uint32_t k) { return b * 8 + (k ^ (b & 7)); }
+
+template <typename AT>
+__device__ __forceinline__ void stage_a(const AT* __restrict__ a, float* sa, uint32_t K);
+template <>
+__device__ __forceinline__ void stage_a<float>(const float* __restrict__ a, float* sa, uint32_t K) {
+  // K is a multiple of 32: float4 copies, every load of a thread issued first
+  const float4* a4 = reinterpret_cast<const float4*>(a);
+  float4* s4 = reinterpret_cast<float4*>(sa);
+  const uint32_t n4 = K / 4;
+  for (uint32_t i0 = threadIdx.x; i0 < n4; i0 += 8 * GEMV_THREADS) {
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const uint32_t i = i0 + (uint32_t)u * GEMV_THREADS;
+      if (i < n4) v[u] = __ldg(a4 + i);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const uint32_t i = i0 + (uint32_t)u * GEMV_THREADS;
+      if (i < n4) s4[a_slot(i >> 3, i & 7)] = v[u];
+    }
+  }
+}
+template <>
+__device__ __forceinline__ void stage_a<__half>(const __half* __restrict__ a, float* sa,
+                                                uint32_t K) {
+  const uint2* a4 = reinterpret_cast<const uint2*>(a);  // 4 halves
+  float4* s4 = reinterpret_cast<float4*>(sa);
+  const uint32_t n4 = K / 4;
+  for (uint32_t i0 = threadIdx.x; i0 < n4; i0 += 8 * GEMV_THREADS) {
+    uint2 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const uint32_t i = i0 + (uint32_t)u * GEMV_THREADS;
+      if (i < n4) v[u] = __ldg(a4 + i);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const uint32_t i = i0 + (uint32_t)u * GEMV_THREADS;
+      if (i < n4) {
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&v[u].x));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&v[u].y));
+        s4[a_slot(i >> 3, i & 7)] = make_float4(lo.x, lo.y, hi.x, hi.y);
+      }
+    }
+  }
+}
+
+// One row (32 blocks, one per lane) of a column group: the lane's block of
+// each of the 4 columns.
+struct RowLoad {
+  uint4 p[CG];
+  float s[CG];
+  uint32_t z[CG];
+};
 
 template <typename AT, int MODE>
 __global__ void __launch_bounds__(GEMV_THREADS)
     q4_gemv_kernel(const AT* __restrict__ a, const GemvArgs args) {
-  extern __shared__ float sa[];  // A as f32 [K], then the per-block sums of A [n_blocks]
-  const uint32_t nb = args.n_blocks, K = nb * 32;
-  float* sasum = sa + K;
-  for (uint32_t i = threadIdx.x; i < K; i += GEMV_THREADS) sa[i] = a_at<AT>(a, i);
+  extern __shared__ float sa[];  // A as f32 [K], float4s swizzled per block
+  const uint32_t nb = args.n_blocks;
+  stage_a<AT>(a, sa, nb * 32);
   __syncthreads();
-  for (uint32_t b = threadIdx.x; b < nb; b += GEMV_THREADS) {
-    float s = 0.f;
-#pragma unroll 8
-    for (int j = 0; j < 32; j++) s += sa[b * 32 + j];
-    sasum[b] = s;
-  }
-  __syncthreads();
+  const float4* sa4 = reinterpret_cast<const float4*>(sa);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t word = (uint32_t)lane & 3u, slot = (uint32_t)lane >> 2;
   const uint32_t n_groups = (args.n_total + CG - 1) / CG;
   const uint32_t n_warps = gridDim.x * (GEMV_THREADS / 32);
+  const uint32_t rows = (nb + 31) / 32;
   for (uint32_t g = blockIdx.x * (GEMV_THREADS / 32) + warp; g < n_groups; g += n_warps) {
     // each column of the group: its matrix (selected without indexing the
     // parameter block) and its first block
-    const uint32_t* Bp[CG];
+    const uint4* Bp[CG];
     const float* Sp[CG];
     const uint32_t* Zp[CG];
-    uint32_t mat[CG], cl[CG];
-    uint64_t base[CG];
+    uint32_t mat[CG], cl[CG], base[CG];
     bool live[CG];
 #pragma unroll
     for (int j = 0; j < CG; j++) {
@@ -117,50 +184,67 @@ __global__ void __launch_bounds__(GEMV_THREADS)
           m = 2;
         }
       }
-      Bp[j] = m == 0 ? args.w[0].B : (m == 1 ? args.w[1].B : args.w[2].B);
+      Bp[j] = reinterpret_cast<const uint4*>(m == 0 ? args.w[0].B
+                                                    : (m == 1 ? args.w[1].B : args.w[2].B));
       Sp[j] = m == 0 ? args.w[0].scales : (m == 1 ? args.w[1].scales : args.w[2].scales);
       Zp[j] = m == 0 ? args.w[0].zp : (m == 1 ? args.w[1].zp : args.w[2].zp);
       mat[j] = m;
       cl[j] = c;
-      base[j] = (uint64_t)c * nb;
+      base[j] = c * nb;  // < 2^32: N * n_blocks of one matrix fits (checked on the host)
     }
+    auto load_row = [&](uint32_t r, RowLoad& L) {
+      const uint32_t blk = r * 32 + (uint32_t)lane;
+#pragma unroll
+      for (int j = 0; j < CG; j++) {
+        if (r < rows && blk < nb && live[j]) {
+          const uint32_t i = base[j] + blk;
+          L.p[j] = __ldg(Bp[j] + i);
+          L.s[j] = __ldg(Sp[j] + i);
+          L.z[j] = (__ldg(Zp[j] + (i >> 3)) >> ((i & 7) * 4)) & 15u;
+        } else {
+          L.p[j] = make_uint4(0, 0, 0, 0);
+          L.s[j] = 0.f;
+          L.z[j] = 0;
+        }
+      }
+    };
     float acc[CG];
 #pragma unroll
     for (int j = 0; j < CG; j++) acc[j] = 0.f;
-    for (uint32_t b0 = 0; b0 < nb; b0 += 8 * UNROLL) {
-      uint32_t p[UNROLL][CG], z[UNROLL][CG];
-      float s[UNROLL][CG];
+    RowLoad buf[DEPTH + 1];
 #pragma unroll
-      for (int u = 0; u < UNROLL; u++) {
-        const uint32_t blk = b0 + (uint32_t)u * 8 + slot;
+    for (int d = 0; d < DEPTH; d++) load_row((uint32_t)d, buf[d]);
+    // rows r, r+1, .., r+DEPTH cycle through the buffers; the loop is unrolled
+    // by DEPTH+1 so every buffer index is a compile-time constant
+    for (uint32_t r0 = 0; r0 < rows; r0 += DEPTH + 1) {
 #pragma unroll
-        for (int j = 0; j < CG; j++) {
-          if (blk < nb && live[j]) {
-            const uint64_t i = base[j] + blk;
-            p[u][j] = __ldg(Bp[j] + i * 4 + word);
-            s[u][j] = __ldg(Sp[j] + i);
-            z[u][j] = (__ldg(Zp[j] + (i >> 3)) >> ((uint32_t)(i & 7) * 4)) & 15u;
-          } else {
-            p[u][j] = 0;
-            s[u][j] = 0.f;
-            z[u][j] = 0;
+      for (int d = 0; d <= DEPTH; d++) {
+        const uint32_t r = r0 + (uint32_t)d;
+        load_row(r + DEPTH, buf[(d + DEPTH) % (DEPTH + 1)]);
+        const RowLoad& L = buf[d];
+        const uint32_t blk = r * 32 + (uint32_t)lane;
+        if (r < rows && blk < nb) {
+          float av[32];
+#pragma unroll
+          for (int k = 0; k < 8; k++) {
+            const float4 v = sa4[a_slot(blk, (uint32_t)k)];
+            av[4 * k] = v.x;
+            av[4 * k + 1] = v.y;
+            av[4 * k + 2] = v.z;
+            av[4 * k + 3] = v.w;
           }
-        }
-      }
+          float t8[8];
 #pragma unroll
-      for (int u = 0; u < UNROLL; u++) {
-        const uint32_t blk = b0 + (uint32_t)u * 8 + slot;
-        if (blk < nb) {
-          const float4 a0 = *reinterpret_cast<const float4*>(sa + blk * 32 + word * 8);
-          const float4 a1 = *reinterpret_cast<const float4*>(sa + blk * 32 + word * 8 + 4);
-          const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-          const float asum = word == 0 ? sasum[blk] : 0.f;  // word 0 carries the zero-point term
+          for (int k = 0; k < 8; k++) t8[k] = (av[4 * k] + av[4 * k + 1]) + (av[4 * k + 2] + av[4 * k + 3]);
+          const float asum = ((t8[0] + t8[1]) + (t8[2] + t8[3])) + ((t8[4] + t8[5]) + (t8[6] + t8[7]));
 #pragma unroll
           for (int j = 0; j < CG; j++) {
-            float d = 0.f;
-#pragma unroll
-            for (int e = 0; e < 8; e++) d = fmaf(av[e], nib_f(p[u][j], e), d);
-            acc[j] = fmaf(s[u][j], d - (float)z[u][j] * asum, acc[j]);
+            float d0 = word_dot(L.p[j].x, av, 0.f);
+            float d1 = word_dot(L.p[j].y, av + 8, 0.f);
+            d0 = word_dot(L.p[j].z, av + 16, d0);
+            d1 = word_dot(L.p[j].w, av + 24, d1);
+            const float dsum = d0 + d1;  // sum_j a_j (1 + q_j/16)
+            acc[j] = fmaf(L.s[j], fmaf(16.f, dsum, -(16.f + (float)L.z[j]) * asum), acc[j]);
           }
         }
       }
@@ -187,8 +271,8 @@ __global__ void __launch_bounds__(GEMV_THREADS)
         if (MODE == OUT_F32) {
           const uint32_t col = g * CG + (uint32_t)lane;
           if (args.epilogue == 1) {
-            const float r = fmaxf(v, 0.f);
-            v = r * r;
+            const float rr = fmaxf(v, 0.f);
+            v = rr * rr;
           } else if (args.epilogue == 2) {
             v = args.y[col] + v;
           }
@@ -204,9 +288,11 @@ __global__ void __launch_bounds__(GEMV_THREADS)
   }
 }
 
-int check_q4(const Q4& w, const char* who, const char* name) {
+int check_q4(const Q4& w, uint32_t n_blocks, const char* who, const char* name) {
   using namespace nwd;
   if (!w.B || !w.scales || !w.zp) return fail(NWD_ERR_INVALID, "%s: null %s weights", who, name);
+  if ((uint64_t)w.N * n_blocks >= (1ull << 32))
+    return fail(NWD_ERR_UNSUPPORTED, "%s: %s has 2^32 blocks or more", who, name);
   if (reinterpret_cast<uintptr_t>(w.B) & 15u)
     return fail(NWD_ERR_INVALID, "%s: %s packed weights must be 16-byte aligned", who, name);
   return NWD_OK;
@@ -227,12 +313,33 @@ int launch_gemv(const AT* a, const GemvArgs& args, void* stream, const char* who
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(q4_gemv_kernel)");
     smem_set[di.device][slot] = true;
   }
+  // one column group per warp where they fit; otherwise as many CTAs as stay
+  // resident, each walking several groups
+  // resident CTAs per SM for this A size, cached per device, kernel and K (a
+  // few K values per process: the engine's projections use two)
+  struct Occ {
+    uint32_t nb;
+    int per_sm;
+  };
+  static Occ cache[64][2][2][4] = {};
+  const int mode_slot = MODE == OUT_F32 ? 0 : 1;
+  Occ* line = cache[di.device < 64 ? di.device : 0][slot][mode_slot];
+  int per_sm = 0;
+  for (int i = 0; i < 4 && !per_sm; i++)
+    if (line[i].nb == args.n_blocks) per_sm = line[i].per_sm;
+  if (!per_sm) {
+    int n = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &n, q4_gemv_kernel<AT, MODE>, GEMV_THREADS, smem_bytes(args.n_blocks));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    per_sm = std::max(1, n);
+    for (int i = 3; i > 0; i--) line[i] = line[i - 1];
+    line[0] = Occ{args.n_blocks, per_sm};
+  }
   const uint32_t groups = (args.n_total + CG - 1) / CG;
   const uint32_t warps = GEMV_THREADS / 32;
-  // enough warps for one column group each, at most 4 CTAs per SM (each CTA
-  // reads A once from L2)
   uint64_t grid = (groups + warps - 1) / warps;
-  grid = std::min<uint64_t>(grid, (uint64_t)di.sm_count * 4);
+  grid = std::min<uint64_t>(grid, (uint64_t)di.sm_count * (uint64_t)per_sm);
   q4_gemv_kernel<AT, MODE><<<(uint32_t)grid, GEMV_THREADS, smem_bytes(args.n_blocks),
                              (cudaStream_t)stream>>>(a, args);
   cudaError_t e = cudaGetLastError();
@@ -265,7 +372,7 @@ int nwd_q4_gemv(const float* a, const uint32_t* b, const float* scales, const ui
   if (epilogue > 2) return fail(NWD_ERR_INVALID, "%s: epilogue %u (0, 1 or 2)", who, epilogue);
   GemvArgs args{};
   args.w[0] = Q4{b, scales, zp, N};
-  if ((st = check_q4(args.w[0], who, "the"))) return st;
+  if ((st = check_q4(args.w[0], n_blocks, who, "the"))) return st;
   if (N == 0) return ok();
   args.n_mats = 1;
   args.n_total = N;
@@ -285,7 +392,7 @@ int nwd_q4_gemv_f16a(const uint16_t* a, const uint32_t* b, const float* scales,
   if (epilogue > 2) return fail(NWD_ERR_INVALID, "%s: epilogue %u (0, 1 or 2)", who, epilogue);
   GemvArgs args{};
   args.w[0] = Q4{b, scales, zp, N};
-  if ((st = check_q4(args.w[0], who, "the"))) return st;
+  if ((st = check_q4(args.w[0], n_blocks, who, "the"))) return st;
   if (N == 0) return ok();
   args.n_mats = 1;
   args.n_total = N;
@@ -313,8 +420,8 @@ int nwd_q4_qkv_append(const float* h, const uint32_t* bq, const float* sq, const
   args.w[0] = Q4{bq, sq, zq, n_heads * head_dim};
   args.w[1] = Q4{bk, sk, zk, row};
   args.w[2] = Q4{bv, sv, zv, row};
-  if ((st = check_q4(args.w[0], who, "q")) || (st = check_q4(args.w[1], who, "k")) ||
-      (st = check_q4(args.w[2], who, "v")))
+  if ((st = check_q4(args.w[0], n_blocks, who, "q")) || (st = check_q4(args.w[1], n_blocks, who, "k")) ||
+      (st = check_q4(args.w[2], n_blocks, who, "v")))
     return st;
   args.n_mats = 3;
   args.n_total = args.w[0].N + 2 * row;
