@@ -219,7 +219,7 @@ int nwd_attn_merge_packed(const float* packed, uint16_t* o, uint32_t shards, uin
  * b = [N][n_blocks][4] u32 (32 values per block, element j of a word in bits
  * [4j, 4j+4), 16-byte aligned), scales = [N][n_blocks] f32, zp = 4-bit zero
  * points packed 8 per u32, nibble n*n_blocks + blk.  Element value
- * (q - zero) * scale; K must be 32 * n_blocks (at most 32768).  epilogue:
+ * (q - zero) * scale; K must be 32 * n_blocks (at most 14080).  epilogue:
  * 0 = store, 1 = relu2 (matmul_nbits_sg.wgsl:76-79, the MLP up projection),
  * 2 = Y[n] += result (the residual add of kernels/add.wgsl fused, as
  * runtime.js:392-393 applies it after o_proj). */

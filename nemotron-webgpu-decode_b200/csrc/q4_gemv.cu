@@ -10,20 +10,35 @@
 // block ([N][n_blocks]) and one 4-bit zero point per block (packed 8 per u32,
 // nibble n*n_blocks + blk).  Element value (q - zero) * scale.
 //
-// HBM-bound: a column's weights are read once (20.5 bytes per 32 elements).
-// A warp takes a group of 4 columns and walks them in rows of 32 blocks, one
-// block per lane: for each column a lane loads the block's 16 bytes, its scale
-// and its zero point, so a row is 512 contiguous bytes per column.  The loads
-// of the next two rows are in flight while a row is computed (software
-// pipelining) and the grid is sized to what stays resident.  The lane's 32
-// activations come from a shared-memory copy of A (float4s XOR-swizzled by
-// block, so the 32 lanes of a warp, reading 32 different blocks, hit distinct
-// banks) and serve all 4 columns.  A nibble q becomes the float 1 + q/16 with a
-// shift and one logic operation (q placed in the top mantissa bits), so
-//   sum_j a_j q_j = 16 * (sum_j a_j (1 + q_j/16) - sum_j a_j)
-// and a block contributes scale * (16 * sum_j a_j f_j - (16 + zero) * sum_j a_j):
-// three instructions per element, none through the special-function unit.
-// f32 accumulation; lanes are reduced with shuffles at the end of the group.
+// A column's weights are read once (20.5 bytes per 32 elements); the kernel is
+// built so that every byte a CTA needs is in flight at once and the inner loop
+// is as short as possible.  The products run on the tensor cores (mma.sync
+// m16n8k16, f16 in, f32 accumulate):
+//   * A (16 x 16) = the weights of 16 output columns: lane (g, t) = (lane / 4,
+//     lane % 4) takes word t of the block of columns g and g + 8 and turns its
+//     8 nibbles into exact fp16 integers q - zero: a masked OR against an fp16
+//     exponent per nibble pair (1024 + q for the nibbles at bits 0-3 of each
+//     half, 64 + q for those at bits 4-7, where the fp16 step is 1/16), then
+//     one half2 subtract of (1024 + zero) or (64 + zero).  The reduction index
+//     of the MMA is permuted so these pairs are exactly the A fragment's: in
+//     step s of a block, k = (2t, 2t+1) holds elements (8t+2s, 8t+2s+4) and
+//     k = (2t+8, 2t+9) holds (8t+2s+1, 8t+2s+5).
+//   * B (16 x 8) = the activations in the same permuted order: column 0 =
+//     fp16(a), column 1 = fp16(a - fp16(a)), the rest zero, so a * (q - zero)
+//     keeps ~22 bits and the sum is f32.  Lanes 0-7 supply them.
+//   * D row r = output column r of the tile: column 0 its dot with fp16(a),
+//     column 1 with the remainder.  Per block both times the block scale go
+//     into two f32 accumulators.
+// A CTA owns 16 columns.  Its 256 threads first copy everything the tile reads
+// (the columns' weights and scales, their zero point words, the activations)
+// from global into shared memory with cp.async, all at once and lane-dense
+// (a warp copies two whole columns; the activations and zero point words are
+// spread over all threads).  After one wait and one barrier they build, in one
+// pass, the B fragments (in place over the raw activations) and a table of the
+// fp16 (1024 + zero, 64 + zero) pairs per (column, block).  The 8 warps then
+// split the blocks (K) in eighths; the loop body is shared-memory loads, the
+// nibble unpacking, two MMAs and four FMAs.  The 8 warps' sums meet in shared
+// memory in a fixed order (deterministic).
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -32,11 +47,51 @@
 
 namespace {
 
-constexpr int GEMV_THREADS = 128;      // 4 warps
-constexpr int CG = 4;                  // columns per warp
-constexpr int DEPTH = 2;               // rows of 32 blocks in flight ahead of the one computed
-constexpr uint32_t MAX_BLOCKS = 1024;  // K <= 32768 (shared-memory copy of A)
-constexpr size_t smem_bytes(uint32_t n_blocks) { return (size_t)n_blocks * 32 * sizeof(float); }
+constexpr int GEMV_WARPS = 8;
+constexpr int GEMV_THREADS = GEMV_WARPS * 32;
+constexpr uint32_t TILE_N = 16;       // output columns per CTA (the MMA's M)
+constexpr uint32_t MAX_BLOCKS = 440;  // K <= 14080 (a tile's shared memory stays under 227 KB)
+
+// Shared memory of a CTA (all offsets multiples of 16 bytes):
+//   W    [16][cs][16 B]  the columns' packed weights; the column stride is an
+//                        odd number of blocks, so the 8 columns of a word read
+//                        hit distinct banks
+//   S    [nb][8] float2  the block scales of columns (g, g + 8)
+//   A    [nb][128 B]     per block: the raw activations as copied, then the B
+//                        fragments made from them in place (uint4 [row][t])
+//   ZT   [nb][8] uint2   the fp16 pair (1024 + zero, 64 + zero) of columns
+//                        (g, g + 8)
+//   ZC   [16][zc]        each column's zero point words as copied
+//   COLS [16]            where each column's data starts
+//   ZERO 16 bytes        the B fragment of lanes 8-31
+//   RED  [warp][16] f32  the warps' sums
+struct ColSm {
+  const uint8_t* w;   // packed weights of the column
+  const float* s;     // its scales
+  const uint32_t* z;  // the zero point array of its matrix
+  uint32_t c;         // column within its matrix
+  uint32_t live;
+  uint32_t pad[4];
+};
+static_assert(sizeof(ColSm) == 48, "ColSm size");
+
+__host__ __device__ constexpr uint32_t col_stride_blocks(uint32_t nb) { return nb | 1u; }
+// words spanned by a column's nb nibbles, wherever they start
+__host__ __device__ constexpr uint32_t zc_words(uint32_t nb) { return nb / 8 + 2; }
+__host__ __device__ constexpr size_t round16(size_t x) { return (x + 15) / 16 * 16; }
+__host__ __device__ constexpr size_t off_s(uint32_t nb) { return (size_t)TILE_N * col_stride_blocks(nb) * 16; }
+__host__ __device__ constexpr size_t off_a(uint32_t nb) { return off_s(nb) + (size_t)nb * 64; }
+__host__ __device__ constexpr size_t off_zt(uint32_t nb) { return off_a(nb) + (size_t)nb * 128; }
+__host__ __device__ constexpr size_t off_zc(uint32_t nb) { return off_zt(nb) + (size_t)nb * 64; }
+__host__ __device__ constexpr size_t off_cols(uint32_t nb) {
+  return off_zc(nb) + round16((size_t)TILE_N * zc_words(nb) * 4);
+}
+__host__ __device__ constexpr size_t off_zero(uint32_t nb) { return off_cols(nb) + TILE_N * sizeof(ColSm); }
+__host__ __device__ constexpr size_t off_red(uint32_t nb) { return off_zero(nb) + 16; }
+__host__ __device__ constexpr size_t smem_bytes(uint32_t nb) {
+  return off_red(nb) + (size_t)GEMV_WARPS * TILE_N * 4;
+}
+static_assert(smem_bytes(MAX_BLOCKS) <= 227 * 1024, "tile shared memory");
 
 enum OutMode : int {
   OUT_F32 = 0,  // Y[n] (epilogue 0), relu2 (1), Y[n] += (2)
@@ -62,227 +117,233 @@ struct GemvArgs {
   __half* v_row;
 };
 
-// 1 + q/16 for the 4-bit field q at bits [4E, 4E+4) of x: q moved to mantissa
-// bits 19-22 under the exponent of 1.0 (exact).  The move is an integer
-// multiply (by 2^s, or the high word of a multiply by 2^(32-s)), which runs on
-// the FMA pipe; only the mask-and-merge uses the integer ALU, which has half
-// the FMA pipe's throughput and would otherwise bound the kernel.
-template <int E>
-__device__ __forceinline__ float nib16(uint32_t x) {
-  constexpr int sh = 19 - 4 * E;
-  uint32_t t;
-  if (sh >= 0) {
-    asm("mul.lo.u32 %0, %1, %2;" : "=r"(t) : "r"(x), "n"(1u << (sh >= 0 ? sh : 0)));
-  } else {
-    asm("mul.hi.u32 %0, %1, %2;" : "=r"(t) : "r"(x), "n"(1u << (sh < 0 ? 32 + sh : 0)));
+__device__ __forceinline__ uint32_t lop3_or_and(uint32_t x, uint32_t mask, uint32_t magic) {
+  uint32_t r;  // (x & mask) | magic
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(x), "r"(mask), "r"(magic));
+  return r;
+}
+__device__ __forceinline__ uint32_t h2_bits(__half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
+__device__ __forceinline__ uint32_t pack_h2(__half lo, __half hi) {
+  return h2_bits(__halves2half2(lo, hi));
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1,
+                                         const float (&c)[4]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%11,%12,%13};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]),
+        "f"(c[3]));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// a column of the tile resolved to its matrix (selected without indexing the
+// parameter block) and local column
+__device__ __forceinline__ ColSm col_ref(const GemvArgs& args, uint32_t col) {
+  ColSm r{};
+  r.live = col < args.n_total;
+  uint32_t m = 0, c = r.live ? col : 0;
+  if (c >= args.w[0].N && args.n_mats > 1) {
+    c -= args.w[0].N;
+    m = 1;
+    if (c >= args.w[1].N && args.n_mats > 2) {
+      c -= args.w[1].N;
+      m = 2;
+    }
   }
-  return __uint_as_float((t & 0x00780000u) | 0x3F800000u);
+  const uint32_t* B = m == 0 ? args.w[0].B : (m == 1 ? args.w[1].B : args.w[2].B);
+  const float* S = m == 0 ? args.w[0].scales : (m == 1 ? args.w[1].scales : args.w[2].scales);
+  r.z = m == 0 ? args.w[0].zp : (m == 1 ? args.w[1].zp : args.w[2].zp);
+  r.w = reinterpret_cast<const uint8_t*>(B) + (size_t)c * args.n_blocks * 16;
+  r.s = S + (size_t)c * args.n_blocks;
+  r.c = c;
+  return r;
 }
 
-// the 8 values of one weight word against 8 activations
-__device__ __forceinline__ float word_dot(uint32_t x, const float* a, float d) {
-  d = fmaf(a[0], nib16<0>(x), d);
-  d = fmaf(a[1], nib16<1>(x), d);
-  d = fmaf(a[2], nib16<2>(x), d);
-  d = fmaf(a[3], nib16<3>(x), d);
-  d = fmaf(a[4], nib16<4>(x), d);
-  d = fmaf(a[5], nib16<5>(x), d);
-  d = fmaf(a[6], nib16<6>(x), d);
-  d = fmaf(a[7], nib16<7>(x), d);
-  return d;
-}
-
-// shared-memory slot of float4 k (0..7) of block b
-__device__ __forceinline__ uint32_t a_slot(uint32_t b, uint32_t k) { return b * 8 + (k ^ (b & 7)); }
-
+// The 8 activations [8t, 8t + 8) of a block, read from its raw copy.
 template <typename AT>
-__device__ __forceinline__ void stage_a(const AT* __restrict__ a, float* sa, uint32_t K);
+__device__ __forceinline__ void read_act(const uint8_t* blk, uint32_t t, float (&x)[8]);
 template <>
-__device__ __forceinline__ void stage_a<float>(const float* __restrict__ a, float* sa, uint32_t K) {
-  // K is a multiple of 32: float4 copies, every load of a thread issued first
-  const float4* a4 = reinterpret_cast<const float4*>(a);
-  float4* s4 = reinterpret_cast<float4*>(sa);
-  const uint32_t n4 = K / 4;
-  for (uint32_t i0 = threadIdx.x; i0 < n4; i0 += 8 * GEMV_THREADS) {
-    float4 v[8];
-#pragma unroll
-    for (int u = 0; u < 8; u++) {
-      const uint32_t i = i0 + (uint32_t)u * GEMV_THREADS;
-      if (i < n4) v[u] = __ldg(a4 + i);
-    }
-#pragma unroll
-    for (int u = 0; u < 8; u++) {
-      const uint32_t i = i0 + (uint32_t)u * GEMV_THREADS;
-      if (i < n4) s4[a_slot(i >> 3, i & 7)] = v[u];
-    }
-  }
+__device__ __forceinline__ void read_act<float>(const uint8_t* blk, uint32_t t, float (&x)[8]) {
+  const float4 u = reinterpret_cast<const float4*>(blk + 32 * t)[0];
+  const float4 v = reinterpret_cast<const float4*>(blk + 32 * t)[1];
+  x[0] = u.x; x[1] = u.y; x[2] = u.z; x[3] = u.w;
+  x[4] = v.x; x[5] = v.y; x[6] = v.z; x[7] = v.w;
 }
 template <>
-__device__ __forceinline__ void stage_a<__half>(const __half* __restrict__ a, float* sa,
-                                                uint32_t K) {
-  const uint2* a4 = reinterpret_cast<const uint2*>(a);  // 4 halves
-  float4* s4 = reinterpret_cast<float4*>(sa);
-  const uint32_t n4 = K / 4;
-  for (uint32_t i0 = threadIdx.x; i0 < n4; i0 += 8 * GEMV_THREADS) {
-    uint2 v[8];
+__device__ __forceinline__ void read_act<__half>(const uint8_t* blk, uint32_t t, float (&x)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(blk + 16 * t);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int u = 0; u < 8; u++) {
-      const uint32_t i = i0 + (uint32_t)u * GEMV_THREADS;
-      if (i < n4) v[u] = __ldg(a4 + i);
-    }
-#pragma unroll
-    for (int u = 0; u < 8; u++) {
-      const uint32_t i = i0 + (uint32_t)u * GEMV_THREADS;
-      if (i < n4) {
-        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&v[u].x));
-        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&v[u].y));
-        s4[a_slot(i >> 3, i & 7)] = make_float4(lo.x, lo.y, hi.x, hi.y);
-      }
-    }
+  for (int j = 0; j < 4; j++) {
+    const __half2 h = bits_h2(w[j]);
+    x[2 * j] = __low2float(h);
+    x[2 * j + 1] = __high2float(h);
   }
 }
-
-// One row (32 blocks, one per lane) of a column group: the lane's block of
-// each of the 4 columns.
-struct RowLoad {
-  uint4 p[CG];
-  float s[CG];
-  uint32_t z[CG];
-};
 
 template <typename AT, int MODE>
-__global__ void __launch_bounds__(GEMV_THREADS)
+__global__ void __launch_bounds__(GEMV_THREADS, 4)
     q4_gemv_kernel(const AT* __restrict__ a, const GemvArgs args) {
-  extern __shared__ float sa[];  // A as f32 [K], float4s swizzled per block
-  const uint32_t nb = args.n_blocks;
-  stage_a<AT>(a, sa, nb * 32);
-  __syncthreads();
-  const float4* sa4 = reinterpret_cast<const float4*>(sa);
+  extern __shared__ __align__(16) uint8_t smem[];
+  const uint32_t nb = args.n_blocks, cs = col_stride_blocks(nb), zc = zc_words(nb);
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(smem);
+  ColSm* cols = reinterpret_cast<ColSm*>(smem + off_cols(nb));
+  float* red = reinterpret_cast<float*>(smem + off_red(nb));
+  const uint32_t* zcw = reinterpret_cast<const uint32_t*>(smem + off_zc(nb));
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t n_groups = (args.n_total + CG - 1) / CG;
-  const uint32_t n_warps = gridDim.x * (GEMV_THREADS / 32);
-  const uint32_t rows = (nb + 31) / 32;
-  for (uint32_t g = blockIdx.x * (GEMV_THREADS / 32) + warp; g < n_groups; g += n_warps) {
-    // each column of the group: its matrix (selected without indexing the
-    // parameter block) and its first block
-    const uint4* Bp[CG];
-    const float* Sp[CG];
-    const uint32_t* Zp[CG];
-    uint32_t mat[CG], cl[CG], base[CG];
-    bool live[CG];
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t g = lane >> 2, t = lane & 3;
+  const uint32_t tile = blockIdx.x;
+
+  if (threadIdx.x < TILE_N) cols[threadIdx.x] = col_ref(args, tile * TILE_N + threadIdx.x);
+  if (threadIdx.x == TILE_N)
+    *reinterpret_cast<uint4*>(smem + off_zero(nb)) = make_uint4(0u, 0u, 0u, 0u);
+  __syncthreads();
+
+  // ---- every copy of the tile, in flight at once ----
+  // warp w copies columns w and w + 8: weights and scales one block per lane,
+  // then the words holding the column's zero points
 #pragma unroll
-    for (int j = 0; j < CG; j++) {
-      const uint32_t col = g * CG + (uint32_t)j;
-      live[j] = col < args.n_total;
-      uint32_t m = 0, c = live[j] ? col : 0;
-      if (c >= args.w[0].N && args.n_mats > 1) {
-        c -= args.w[0].N;
-        m = 1;
-        if (c >= args.w[1].N && args.n_mats > 2) {
-          c -= args.w[1].N;
-          m = 2;
-        }
-      }
-      Bp[j] = reinterpret_cast<const uint4*>(m == 0 ? args.w[0].B
-                                                    : (m == 1 ? args.w[1].B : args.w[2].B));
-      Sp[j] = m == 0 ? args.w[0].scales : (m == 1 ? args.w[1].scales : args.w[2].scales);
-      Zp[j] = m == 0 ? args.w[0].zp : (m == 1 ? args.w[1].zp : args.w[2].zp);
-      mat[j] = m;
-      cl[j] = c;
-      base[j] = c * nb;  // < 2^32: N * n_blocks of one matrix fits (checked on the host)
+  for (uint32_t h = 0; h < 2; h++) {
+    const uint32_t j = warp + 8 * h;
+    const ColSm cr = cols[j];
+    if (!cr.live) continue;
+    const uint32_t w_dst = sbase + j * cs * 16;
+    const uint32_t s_dst = sbase + (uint32_t)off_s(nb) + ((j & 7) * 2 + (j >> 3)) * 4;
+    for (uint32_t b = lane; b < nb; b += 32) {
+      cp_async16(w_dst + b * 16, cr.w + (size_t)b * 16);
+      cp_async4(s_dst + b * 64, cr.s + b);
     }
-    auto load_row = [&](uint32_t r, RowLoad& L) {
-      const uint32_t blk = r * 32 + (uint32_t)lane;
-#pragma unroll
-      for (int j = 0; j < CG; j++) {
-        if (r < rows && blk < nb && live[j]) {
-          const uint32_t i = base[j] + blk;
-          L.p[j] = __ldg(Bp[j] + i);
-          L.s[j] = __ldg(Sp[j] + i);
-          L.z[j] = (__ldg(Zp[j] + (i >> 3)) >> ((i & 7) * 4)) & 15u;
-        } else {
-          L.p[j] = make_uint4(0, 0, 0, 0);
-          L.s[j] = 0.f;
-          L.z[j] = 0;
-        }
-      }
-    };
-    float acc[CG];
-#pragma unroll
-    for (int j = 0; j < CG; j++) acc[j] = 0.f;
-    RowLoad buf[DEPTH + 1];
-#pragma unroll
-    for (int d = 0; d < DEPTH; d++) load_row((uint32_t)d, buf[d]);
-    // rows r, r+1, .., r+DEPTH cycle through the buffers; the loop is unrolled
-    // by DEPTH+1 so every buffer index is a compile-time constant
-    for (uint32_t r0 = 0; r0 < rows; r0 += DEPTH + 1) {
-#pragma unroll
-      for (int d = 0; d <= DEPTH; d++) {
-        const uint32_t r = r0 + (uint32_t)d;
-        load_row(r + DEPTH, buf[(d + DEPTH) % (DEPTH + 1)]);
-        const RowLoad& L = buf[d];
-        const uint32_t blk = r * 32 + (uint32_t)lane;
-        if (r < rows && blk < nb) {
-          float av[32];
-#pragma unroll
-          for (int k = 0; k < 8; k++) {
-            const float4 v = sa4[a_slot(blk, (uint32_t)k)];
-            av[4 * k] = v.x;
-            av[4 * k + 1] = v.y;
-            av[4 * k + 2] = v.z;
-            av[4 * k + 3] = v.w;
-          }
-          float t8[8];
-#pragma unroll
-          for (int k = 0; k < 8; k++) t8[k] = (av[4 * k] + av[4 * k + 1]) + (av[4 * k + 2] + av[4 * k + 3]);
-          const float asum = ((t8[0] + t8[1]) + (t8[2] + t8[3])) + ((t8[4] + t8[5]) + (t8[6] + t8[7]));
-#pragma unroll
-          for (int j = 0; j < CG; j++) {
-            float d0 = word_dot(L.p[j].x, av, 0.f);
-            float d1 = word_dot(L.p[j].y, av + 8, 0.f);
-            d0 = word_dot(L.p[j].z, av + 16, d0);
-            d1 = word_dot(L.p[j].w, av + 24, d1);
-            const float dsum = d0 + d1;  // sum_j a_j (1 + q_j/16)
-            acc[j] = fmaf(L.s[j], fmaf(16.f, dsum, -(16.f + (float)L.z[j]) * asum), acc[j]);
-          }
-        }
-      }
+    const uint32_t w0 = (cr.c * nb) >> 3, n_w = ((cr.c * nb + nb - 1) >> 3) - w0 + 1;
+    for (uint32_t k = lane; k < n_w; k += 32)
+      cp_async4(sbase + (uint32_t)off_zc(nb) + (j * zc + k) * 4, cr.z + w0 + k);
+  }
+  // the activations: 16-byte pieces of each block's 128-byte slot
+  {
+    constexpr uint32_t PIECES = sizeof(AT) * 32 / 16;  // 8 (f32) or 4 (f16)
+    constexpr uint32_t ELEMS = 16 / sizeof(AT);
+    for (uint32_t i = threadIdx.x; i < nb * PIECES; i += GEMV_THREADS) {
+      const uint32_t b = i / PIECES, piece = i % PIECES;
+      cp_async16(sbase + (uint32_t)off_a(nb) + b * 128 + piece * 16, a + (size_t)i * ELEMS);
     }
+  }
+  cp_async_wait_all();
+  __syncthreads();
+
+  // ---- B fragments in place over the raw activations: lane (block, t) turns
+  // elements [8t, 8t + 8) into uint4 [row][t] of its block; a warp's 8 blocks
+  // per round are its own, so a warp barrier separates the reads and writes
+  for (uint32_t base = warp * 32; base < nb * 4; base += GEMV_THREADS) {
+    const uint32_t item = base + lane, bb = item >> 2, tt = item & 3;
+    const bool on = item < nb * 4;
+    uint8_t* blk = smem + off_a(nb) + (size_t)bb * 128;
+    float x[8];
+    if (on) read_act<AT>(blk, tt, x);
+    __syncwarp();
+    if (on) {
+      __half hi[8], lo[8];
 #pragma unroll
-    for (int j = 0; j < CG; j++) {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+      for (int j = 0; j < 8; j++) {
+        hi[j] = __float2half_rn(x[j]);
+        lo[j] = __float2half_rn(x[j] - __half2float(hi[j]));
+      }
+      // step s: {(e, e+4), (e+1, e+5)} with e = 2s
+      reinterpret_cast<uint4*>(blk)[tt] = make_uint4(pack_h2(hi[0], hi[4]), pack_h2(hi[1], hi[5]),
+                                                     pack_h2(hi[2], hi[6]), pack_h2(hi[3], hi[7]));
+      reinterpret_cast<uint4*>(blk)[4 + tt] = make_uint4(pack_h2(lo[0], lo[4]), pack_h2(lo[1], lo[5]),
+                                                         pack_h2(lo[2], lo[6]), pack_h2(lo[3], lo[7]));
     }
-    if (lane < CG) {
-      // lane j writes column j of the group (static register choices per lane)
-      float v = acc[0];
-      bool lv = live[0];
-      uint32_t m = mat[0], c = cl[0];
+    __syncwarp();
+  }
+  // ---- the zero point table: (block, column) -> fp16 pair (1024 + z, 64 + z)
+  {
+    uint32_t* zt = reinterpret_cast<uint32_t*>(smem + off_zt(nb));
+    const uint32_t j = threadIdx.x & 15;
+    const uint32_t c = cols[j].c, live = cols[j].live, i0 = c * nb;
+    for (uint32_t b = threadIdx.x >> 4; b < nb; b += GEMV_THREADS / 16) {
+      const uint32_t i = i0 + b;
+      const uint32_t z = live ? (zcw[j * zc + (i >> 3) - (i0 >> 3)] >> ((i & 7) * 4)) & 15u : 0u;
+      zt[(b * 8 + (j & 7)) * 2 + (j >> 3)] = (0x6400u | z) | ((0x5400u | (z << 4)) << 16);
+    }
+  }
+  __syncthreads();
+
+  // ---- this warp's eighth of the blocks ----
+  const uint32_t b_lo = nb * warp / GEMV_WARPS, b_hi = nb * (warp + 1) / GEMV_WARPS;
+  const uint32_t* ws = reinterpret_cast<const uint32_t*>(smem);
+  const float2* ss = reinterpret_cast<const float2*>(smem + off_s(nb));
+  const uint2* zt2 = reinterpret_cast<const uint2*>(smem + off_zt(nb));
+  // lanes 0-7 read their B fragment of each block, lanes 8-31 a zero one
+  const uint8_t* fbase = lane < 8 ? smem + off_a(nb) + lane * 16 : smem + off_zero(nb);
+  const uint32_t fstride = lane < 8 ? 128u : 0u;
+  float accH0 = 0.f, accL0 = 0.f, accH1 = 0.f, accL1 = 0.f;  // columns g and g + 8
+  const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
+  for (uint32_t b = b_lo; b < b_hi; b++) {
+    const uint32_t x0 = ws[(g * cs + b) * 4 + t];
+    const uint32_t x1 = ws[((g + 8) * cs + b) * 4 + t];
+    const uint2 zu = zt2[b * 8 + g];
+    const uint4 f = *reinterpret_cast<const uint4*>(fbase + b * fstride);
+    const float2 sc = ss[b * 8 + g];
+    const __half2 zl0 = __low2half2(bits_h2(zu.x)), zh0 = __high2half2(bits_h2(zu.x));
+    const __half2 zl1 = __low2half2(bits_h2(zu.y)), zh1 = __high2half2(bits_h2(zu.y));
+    const uint32_t x0s = x0 >> 8, x1s = x1 >> 8;
+    float d[4];
+    mma16816(d, h2_bits(__hsub2(bits_h2(lop3_or_and(x0, 0x000F000Fu, 0x64006400u)), zl0)),
+             h2_bits(__hsub2(bits_h2(lop3_or_and(x1, 0x000F000Fu, 0x64006400u)), zl1)),
+             h2_bits(__hsub2(bits_h2(lop3_or_and(x0, 0x00F000F0u, 0x54005400u)), zh0)),
+             h2_bits(__hsub2(bits_h2(lop3_or_and(x1, 0x00F000F0u, 0x54005400u)), zh1)), f.x, f.y,
+             zero4);
+    mma16816(d, h2_bits(__hsub2(bits_h2(lop3_or_and(x0s, 0x000F000Fu, 0x64006400u)), zl0)),
+             h2_bits(__hsub2(bits_h2(lop3_or_and(x1s, 0x000F000Fu, 0x64006400u)), zl1)),
+             h2_bits(__hsub2(bits_h2(lop3_or_and(x0s, 0x00F000F0u, 0x54005400u)), zh0)),
+             h2_bits(__hsub2(bits_h2(lop3_or_and(x1s, 0x00F000F0u, 0x54005400u)), zh1)), f.z, f.w,
+             d);
+    accH0 = fmaf(sc.x, d[0], accH0);
+    accL0 = fmaf(sc.x, d[1], accL0);
+    accH1 = fmaf(sc.y, d[2], accH1);
+    accL1 = fmaf(sc.y, d[3], accL1);
+  }
+  // lanes t == 0 hold columns g and g + 8 (D columns 0 and 1; the rest are zero)
+  if (t == 0) {
+    red[warp * TILE_N + g] = accH0 + accL0;
+    red[warp * TILE_N + g + 8] = accH1 + accL1;
+  }
+  __syncthreads();
+  if (threadIdx.x < TILE_N) {
+    const uint32_t j = threadIdx.x;
+    float v = red[j];
 #pragma unroll
-      for (int jj = 1; jj < CG; jj++)
-        if (lane == jj) {
-          v = acc[jj];
-          lv = live[jj];
-          m = mat[jj];
-          c = cl[jj];
+    for (int w = 1; w < GEMV_WARPS; w++) v += red[w * TILE_N + j];
+    const ColSm& cr = cols[j];
+    if (cr.live) {
+      const uint32_t col = tile * TILE_N + j;
+      if (MODE == OUT_F32) {
+        if (args.epilogue == 1) {
+          const float rr = fmaxf(v, 0.f);
+          v = rr * rr;
+        } else if (args.epilogue == 2) {
+          v = args.y[col] + v;
         }
-      if (lv) {
-        if (MODE == OUT_F32) {
-          const uint32_t col = g * CG + (uint32_t)lane;
-          if (args.epilogue == 1) {
-            const float rr = fmaxf(v, 0.f);
-            v = rr * rr;
-          } else if (args.epilogue == 2) {
-            v = args.y[col] + v;
-          }
-          args.y[col] = v;
-        } else {
-          const __half h = __float2half_rn(v);
-          if (m == 0) args.q_out[c] = h;
-          else if (m == 1) args.k_row[c] = h;
-          else args.v_row[c] = h;
-        }
+        args.y[col] = v;
+      } else {
+        const __half h = __float2half_rn(v);
+        if (col < args.w[0].N) args.q_out[cr.c] = h;
+        else if (col < args.w[0].N + args.w[1].N) args.k_row[cr.c] = h;
+        else args.v_row[cr.c] = h;
       }
     }
   }
@@ -304,42 +365,17 @@ int launch_gemv(const AT* a, const GemvArgs& args, void* stream, const char* who
   DeviceInfo di;
   int st = current_device_info(&di);
   if (st) return st;
-  static bool smem_set[64][2] = {};
-  const int slot = (int)sizeof(AT) == 2 ? 1 : 0;
-  if (di.device < 64 && !smem_set[di.device][slot]) {
+  static bool smem_set[64] = {};  // per instantiation (A type, output mode) and device
+  if (di.device < 64 && !smem_set[di.device]) {
     cudaError_t e = cudaFuncSetAttribute(q4_gemv_kernel<AT, MODE>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem_bytes(MAX_BLOCKS));
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(q4_gemv_kernel)");
-    smem_set[di.device][slot] = true;
+    smem_set[di.device] = true;
   }
-  // one column group per warp where they fit; otherwise as many CTAs as stay
-  // resident, each walking several groups
-  // resident CTAs per SM for this A size, cached per device, kernel and K (a
-  // few K values per process: the engine's projections use two)
-  struct Occ {
-    uint32_t nb;
-    int per_sm;
-  };
-  static Occ cache[64][2][2][4] = {};
-  const int mode_slot = MODE == OUT_F32 ? 0 : 1;
-  Occ* line = cache[di.device < 64 ? di.device : 0][slot][mode_slot];
-  int per_sm = 0;
-  for (int i = 0; i < 4 && !per_sm; i++)
-    if (line[i].nb == args.n_blocks) per_sm = line[i].per_sm;
-  if (!per_sm) {
-    int n = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &n, q4_gemv_kernel<AT, MODE>, GEMV_THREADS, smem_bytes(args.n_blocks));
-    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-    per_sm = std::max(1, n);
-    for (int i = 3; i > 0; i--) line[i] = line[i - 1];
-    line[0] = Occ{args.n_blocks, per_sm};
-  }
-  const uint32_t groups = (args.n_total + CG - 1) / CG;
-  const uint32_t warps = GEMV_THREADS / 32;
-  uint64_t grid = (groups + warps - 1) / warps;
-  grid = std::min<uint64_t>(grid, (uint64_t)di.sm_count * (uint64_t)per_sm);
+  // one CTA per 16-column tile (the hardware schedules them as SMs free up)
+  const uint64_t grid = (args.n_total + TILE_N - 1) / TILE_N;
+  if (grid > 0x7fffffffull) return fail(NWD_ERR_UNSUPPORTED, "%s: too many columns", who);
   q4_gemv_kernel<AT, MODE><<<(uint32_t)grid, GEMV_THREADS, smem_bytes(args.n_blocks),
                              (cudaStream_t)stream>>>(a, args);
   cudaError_t e = cudaGetLastError();
@@ -347,8 +383,10 @@ int launch_gemv(const AT* a, const GemvArgs& args, void* stream, const char* who
   return ok();
 }
 
-int check_shape(uint32_t K, uint32_t n_blocks, const char* who) {
+int check_shape(const void* a, uint32_t K, uint32_t n_blocks, const char* who) {
   using namespace nwd;
+  if (reinterpret_cast<uintptr_t>(a) & 15u)
+    return fail(NWD_ERR_INVALID, "%s: the activation vector must be 16-byte aligned", who);
   if (n_blocks == 0 || K != n_blocks * 32)
     return fail(NWD_ERR_INVALID, "%s: K (%u) must be 32 * n_blocks (%u)", who, K, n_blocks);
   if (n_blocks > MAX_BLOCKS)
@@ -367,7 +405,7 @@ int nwd_q4_gemv(const float* a, const uint32_t* b, const float* scales, const ui
                 void* stream) {
   const char* who = "nwd_q4_gemv";
   if (!a || !y) return fail(NWD_ERR_INVALID, "%s: null pointer", who);
-  int st = check_shape(K, n_blocks, who);
+  int st = check_shape(a, K, n_blocks, who);
   if (st) return st;
   if (epilogue > 2) return fail(NWD_ERR_INVALID, "%s: epilogue %u (0, 1 or 2)", who, epilogue);
   GemvArgs args{};
@@ -387,7 +425,7 @@ int nwd_q4_gemv_f16a(const uint16_t* a, const uint32_t* b, const float* scales,
                      uint32_t epilogue, void* stream) {
   const char* who = "nwd_q4_gemv_f16a";
   if (!a || !y) return fail(NWD_ERR_INVALID, "%s: null pointer", who);
-  int st = check_shape(K, n_blocks, who);
+  int st = check_shape(a, K, n_blocks, who);
   if (st) return st;
   if (epilogue > 2) return fail(NWD_ERR_INVALID, "%s: epilogue %u (0, 1 or 2)", who, epilogue);
   GemvArgs args{};
@@ -411,7 +449,7 @@ int nwd_q4_qkv_append(const float* h, const uint32_t* bq, const float* sq, const
   if (!h || !q_out || !k_cache || !v_cache) return fail(NWD_ERR_INVALID, "%s: null pointer", who);
   if (seq >= cap) return fail(NWD_ERR_RANGE, "seq %u exceeds maxSeq %u", seq, cap);
   const uint32_t n_blocks = K / 32;
-  int st = check_shape(K, n_blocks, who);
+  int st = check_shape(h, K, n_blocks, who);
   if (st) return st;
   if (n_heads == 0 || n_kv_heads == 0 || head_dim == 0)
     return fail(NWD_ERR_INVALID, "%s: zero shape", who);

@@ -39,13 +39,16 @@ def _close_f32(got, ref, what):
     (3136, 12544, 1),   # MLP up with relu2 (matmul_nbits_sg.wgsl:76-79)
     (12544, 3136, 0),   # MLP down
     (96, 7, 0),         # ragged: N not a multiple of the column group
-    (32, 33, 1),
+    (32, 33, 1),        # one block: only one warp of the CTA has work
+    (14080, 40, 2),     # the largest K
 ])
 def test_q4_gemv_vs_oracle(ops, oracle, K, N, epilogue):
     w, (b, s, z) = _weights(ops, oracle, N, K // 32, seed=K + N)
     a = _act(oracle, K, seed=7 + K)
-    y = ops.q4_gemv(torch.from_numpy(a).cuda(), w, epilogue=epilogue)
-    ref = oracle.q4_gemv(a, b, s, z, epilogue=epilogue)
+    h = _act(oracle, N, seed=9)
+    y = torch.from_numpy(h.copy()).cuda()
+    ops.q4_gemv(torch.from_numpy(a).cuda(), w, y=y, epilogue=epilogue)
+    ref = oracle.q4_gemv(a, b, s, z, epilogue=epilogue, y=h)
     _close_f32(y.cpu().numpy(), ref, f"K={K} N={N} epilogue={epilogue}")
 
 
@@ -67,11 +70,19 @@ def test_q4_gemv_rejects_bad_shapes(ops, oracle):
     a = torch.zeros(63, device="cuda")
     with pytest.raises(ops.NwdError, match="32 \\* n_blocks"):
         ops.q4_gemv(a, w)
+    with pytest.raises(ops.NwdError, match="exceeds 14080"):
+        ops.q4_gemv(torch.zeros(441 * 32, device="cuda"), _weights(ops, oracle, 8, 441, seed=2)[0])
+    # the activations are copied in 16-byte pieces
+    with pytest.raises(ops.NwdError, match="16-byte aligned"):
+        ops.q4_gemv(torch.zeros(65, device="cuda")[1:], _weights(ops, oracle, 8, 2, seed=1)[0])
 
 
-def test_q4_qkv_append(ops, oracle):
+@pytest.mark.parametrize("K,nh,nkv,hd,cap,seq", [
+    (3136, 40, 8, 128, 256, 37),   # the model's attention layer
+    (96, 3, 1, 40, 16, 15),        # column tiles straddling q / k / v, last cache row
+])
+def test_q4_qkv_append(ops, oracle, K, nh, nkv, hd, cap, seq):
     """q / k / v of one token in one launch, k and v written into cache row seq."""
-    K, nh, nkv, hd, cap, seq = 3136, 40, 8, 128, 256, 37
     wq, hq = _weights(ops, oracle, nh * hd, K // 32, seed=11)
     wk, hk = _weights(ops, oracle, nkv * hd, K // 32, seed=12)
     wv, hv = _weights(ops, oracle, nkv * hd, K // 32, seed=13)
@@ -92,7 +103,7 @@ def test_q4_qkv_append(ops, oracle):
     mask = np.ones(cap, bool)
     mask[seq] = False
     assert np.array_equal(bits(dk)[mask], kc[mask]) and np.array_equal(bits(dv)[mask], vc[mask])
-    with pytest.raises(ops.NwdError, match="seq 256 exceeds maxSeq 256"):
+    with pytest.raises(ops.NwdError, match=f"seq {cap} exceeds maxSeq {cap}"):
         ops.q4_qkv_append(torch.from_numpy(h).cuda(), wq, wk, wv, q, dk, dv, cap)
 
 
