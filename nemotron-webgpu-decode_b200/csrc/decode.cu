@@ -260,6 +260,10 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t B = p.seq_len ? p.batch : 1u;
   const uint32_t G = p.group;
+  // launched as a programmatic dependent launch: let the next kernel start
+  // early, and wait for the previous one before touching any memory
+  nwd::pdl_trigger();
+  nwd::pdl_wait();
 
   // ---- plan: row prefix S over sequences (S[b] = rows before b) ----
   if (tid == 0) {
@@ -971,11 +975,11 @@ int launch(const Call& c) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode_kernel)");
     g_smem_set[di.device][ng] = true;
   }
-  if (ng == 2)
-    decode_kernel<2><<<grid, Cfg<2>::NTHR, Cfg<2>::SMEM_BYTES, (cudaStream_t)c.stream>>>(tmk, tmv, p);
-  else
-    decode_kernel<1><<<grid, Cfg<1>::NTHR, Cfg<1>::SMEM_BYTES, (cudaStream_t)c.stream>>>(tmk, tmv, p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e =
+      ng == 2 ? launch_pdl(decode_kernel<2>, dim3(grid), dim3(Cfg<2>::NTHR), Cfg<2>::SMEM_BYTES,
+                           (cudaStream_t)c.stream, tmk, tmv, p)
+              : launch_pdl(decode_kernel<1>, dim3(grid), dim3(Cfg<1>::NTHR), Cfg<1>::SMEM_BYTES,
+                           (cudaStream_t)c.stream, tmk, tmv, p);
   if (e != cudaSuccess) return cuda_fail(e, c.who);
   return ok();
 }

@@ -35,6 +35,38 @@ int kv_tensor_map(CUtensorMap* out, const void* base, uint64_t rows, uint32_t n_
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// ---- programmatic dependent launch ----
+// A kernel launched with launch_pdl() may start while the kernel before it in
+// the stream is still running.  Such a kernel calls pdl_trigger() at entry (so
+// the kernel after it may start early in turn) and pdl_wait() in every CTA, on
+// every path, before it reads or writes memory that another kernel writes or
+// reads: pdl_wait() returns once the previous kernel has completed and its
+// writes are visible.  Before it, only constant inputs (weights) are read.
+// Because every CTA waits, a kernel completes only after the one before it,
+// so ordering stays transitive along the stream.
+#ifdef __CUDACC__
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+#endif
+
 // ---- workspace layout shared by the decode kernels ----
 // [0, 256)            header: error word, scheduler counters
 // [256, +tickets)     uint32 per (sequence, kv head) merge tickets

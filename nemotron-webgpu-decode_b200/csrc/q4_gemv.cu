@@ -39,6 +39,9 @@
 // split the blocks (K) in eighths; the loop body is shared-memory loads, the
 // nibble unpacking, two MMAs and four FMAs.  The 8 warps' sums meet in shared
 // memory in a fixed order (deterministic).
+// Launched as a programmatic dependent launch: the weight copies (constant
+// inputs) are issued before the kernel waits for the previous kernel in the
+// stream, so in a layer they overlap the attention kernel or the previous GEMV.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -208,6 +211,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 4)
   const uint32_t g = lane >> 2, t = lane & 3;
   const uint32_t tile = blockIdx.x;
 
+  nwd::pdl_trigger();  // the next kernel in the stream may start its own weight copies
   if (threadIdx.x < TILE_N) cols[threadIdx.x] = col_ref(args, tile * TILE_N + threadIdx.x);
   if (threadIdx.x == TILE_N)
     *reinterpret_cast<uint4*>(smem + off_zero(nb)) = make_uint4(0u, 0u, 0u, 0u);
@@ -231,6 +235,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 4)
     for (uint32_t k = lane; k < n_w; k += 32)
       cp_async4(sbase + (uint32_t)off_zc(nb) + (j * zc + k) * 4, cr.z + w0 + k);
   }
+  // everything above reads only the weights; the activations (and the outputs)
+  // belong to the kernels around this one
+  nwd::pdl_wait();
   // the activations: 16-byte pieces of each block's 128-byte slot
   {
     constexpr uint32_t PIECES = sizeof(AT) * 32 / 16;  // 8 (f32) or 4 (f16)
@@ -376,9 +383,8 @@ int launch_gemv(const AT* a, const GemvArgs& args, void* stream, const char* who
   // one CTA per 16-column tile (the hardware schedules them as SMs free up)
   const uint64_t grid = (args.n_total + TILE_N - 1) / TILE_N;
   if (grid > 0x7fffffffull) return fail(NWD_ERR_UNSUPPORTED, "%s: too many columns", who);
-  q4_gemv_kernel<AT, MODE><<<(uint32_t)grid, GEMV_THREADS, smem_bytes(args.n_blocks),
-                             (cudaStream_t)stream>>>(a, args);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(q4_gemv_kernel<AT, MODE>, dim3((uint32_t)grid), dim3(GEMV_THREADS),
+                             smem_bytes(args.n_blocks), (cudaStream_t)stream, a, args);
   if (e != cudaSuccess) return cuda_fail(e, who);
   return ok();
 }
