@@ -145,6 +145,14 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ setup
 
+
+def start_clocks(torch, dev, rank):
+    """nvidia-smi sampling of rank 0's GPU (None on the other ranks)."""
+    if rank != 0:
+        return None
+    uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    return ClockSampler(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+
 def import_pkg():
     if REPO not in sys.path:
         sys.path.insert(0, REPO)
@@ -634,9 +642,11 @@ def run_config4(args, ops, torch, dist, dev, rank, world):
             dist.barrier()
         torch.cuda.synchronize()
 
+    sampler = start_clocks(torch, dev, rank)
     for _ in range(args.warmup):
         step()
     barrier()
+    t0 = time.monotonic()
     a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(args.steps):
@@ -644,6 +654,9 @@ def run_config4(args, ops, torch, dist, dev, rank, world):
     e.record()
     e.synchronize()
     barrier()
+    t1 = time.monotonic()
+    if sampler:
+        sampler.stop()
     ms = a.elapsed_time(e)
     # the prefill kernel alone, per-launch events
     R = min(args.steps, 20)
@@ -706,6 +719,7 @@ def run_config4(args, ops, torch, dist, dev, rank, world):
                     "d2h_bytes_per_step": o.numel() * 2 * world},
             "gpu_launches": 2 * args.steps,
             "device_error": err,
+            "clocks": sampler.summary(t0, t1) if sampler else None,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -789,11 +803,13 @@ def run_config6(args, ops, torch, dist, dev, rank, world):
             dist.barrier()
         torch.cuda.synchronize()
 
+    sampler = start_clocks(torch, dev, rank)
     s = 0
     for _ in range(args.warmup):
         graphs[s % WEIGHT_SETS].replay()
         s += 1
     barrier()
+    t0 = time.monotonic()
     a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(args.steps):
@@ -802,6 +818,9 @@ def run_config6(args, ops, torch, dist, dev, rank, world):
     e.record()
     e.synchronize()
     barrier()
+    t1 = time.monotonic()
+    if sampler:
+        sampler.stop()
     ms = a.elapsed_time(e)
     # the q/k/v launch alone (the largest kernel): one launch per layer of every weight
     # copy (12, cold weights) captured in a graph, so the time is the GPU's alone
@@ -888,6 +907,7 @@ def run_config6(args, ops, torch, dist, dev, rank, world):
             "cpu_baseline": cpu,
             "gpu_launches": 12 * args.steps,
             "device_error": err,
+            "clocks": sampler.summary(t0, t1) if sampler else None,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -951,9 +971,11 @@ def run_config5(args, ops, torch, dist, dev, rank, world):
             dist.barrier()
         torch.cuda.synchronize()
 
+    sampler = start_clocks(torch, dev, rank)
     for _ in range(args.warmup):
         sd.step(q, o)
     barrier()
+    t0 = time.monotonic()
     a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(args.steps):
@@ -961,6 +983,9 @@ def run_config5(args, ops, torch, dist, dev, rank, world):
     e.record()
     e.synchronize()
     barrier()
+    t1 = time.monotonic()
+    if sampler:
+        sampler.stop()
     ms = a.elapsed_time(e)
     # roofline of the shard kernel alone (per-launch events, same stream)
     R = min(args.steps, 20)
@@ -1019,6 +1044,7 @@ def run_config5(args, ops, torch, dist, dev, rank, world):
                     "h2d_bytes_per_step": B * HQ * HD * 2, "d2h_bytes_per_step": B * HQ * HD * 2},
             "gpu_launches": 2 * args.steps,
             "device_error": err,
+            "clocks": sampler.summary(t0, t1) if sampler else None,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -29,19 +29,18 @@
 //   * D row r = output column r of the tile: column 0 its dot with fp16(a),
 //     column 1 with the remainder.  Per block both times the block scale go
 //     into two f32 accumulators.
-// A CTA owns 16 columns.  Its 256 threads first copy everything the tile reads
-// (the columns' weights and scales, their zero point words, the activations)
-// from global into shared memory with cp.async, all at once and lane-dense
-// (a warp copies two whole columns; the activations and zero point words are
-// spread over all threads).  After one wait and one barrier they build, in one
-// pass, the B fragments (in place over the raw activations) and a table of the
-// fp16 (1024 + zero, 64 + zero) pairs per (column, block).  The 8 warps then
-// split the blocks (K) in eighths; the loop body is shared-memory loads, the
-// nibble unpacking, two MMAs and four FMAs.  The 8 warps' sums meet in shared
-// memory in a fixed order (deterministic).
-// Launched as a programmatic dependent launch: the weight copies (constant
-// inputs) are issued before the kernel waits for the previous kernel in the
-// stream, so in a layer they overlap the attention kernel or the previous GEMV.
+// A CTA owns 16 columns.  Its 256 threads first put the tile's constant
+// inputs in flight at once with cp.async, lane-dense (a warp copies two whole
+// columns): the zero point words, then the weights and scales.  As soon as the
+// zero point words are in, they build a table of the fp16 (1024 + zero,
+// 64 + zero) pairs per (column, block).  All of this happens before the kernel
+// waits for the previous kernel in the stream (programmatic dependent launch),
+// so in a layer it overlaps the attention kernel or the previous GEMV.  After
+// the wait they load the activations (through L2) and write the B fragments
+// into shared memory, then wait for the weights; the 8 warps split the blocks
+// (K) in eighths, and the loop body is shared-memory loads, the nibble
+// unpacking, two MMAs and four FMAs.  The 8 warps' sums meet in shared memory
+// in a fixed order (deterministic).
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -60,8 +59,7 @@ constexpr uint32_t MAX_BLOCKS = 440;  // K <= 14080 (a tile's shared memory stay
 //                        odd number of blocks, so the 8 columns of a word read
 //                        hit distinct banks
 //   S    [nb][8] float2  the block scales of columns (g, g + 8)
-//   A    [nb][128 B]     per block: the raw activations as copied, then the B
-//                        fragments made from them in place (uint4 [row][t])
+//   A    [nb][128 B]     per block: the B fragments (uint4 [row][t])
 //   ZT   [nb][8] uint2   the fp16 pair (1024 + zero, 64 + zero) of columns
 //                        (g, g + 8)
 //   ZC   [16][zc]        each column's zero point words as copied
@@ -148,8 +146,11 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
 __device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
 }
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// wait until at most n (0 or 1) of this thread's copy groups are still in flight
+__device__ __forceinline__ void cp_async_wait_pending(uint32_t n) {
+  if (n == 0) asm volatile("cp.async.wait_group 0;" ::: "memory");
+  else asm volatile("cp.async.wait_group 1;" ::: "memory");
 }
 
 // a column of the tile resolved to its matrix (selected without indexing the
@@ -175,19 +176,20 @@ __device__ __forceinline__ ColSm col_ref(const GemvArgs& args, uint32_t col) {
   return r;
 }
 
-// The 8 activations [8t, 8t + 8) of a block, read from its raw copy.
+// Eight consecutive activations from global memory, through L2 (another
+// kernel wrote them).
 template <typename AT>
-__device__ __forceinline__ void read_act(const uint8_t* blk, uint32_t t, float (&x)[8]);
+__device__ __forceinline__ void load_act(const AT* p, float (&x)[8]);
 template <>
-__device__ __forceinline__ void read_act<float>(const uint8_t* blk, uint32_t t, float (&x)[8]) {
-  const float4 u = reinterpret_cast<const float4*>(blk + 32 * t)[0];
-  const float4 v = reinterpret_cast<const float4*>(blk + 32 * t)[1];
+__device__ __forceinline__ void load_act<float>(const float* p, float (&x)[8]) {
+  const float4 u = __ldcg(reinterpret_cast<const float4*>(p));
+  const float4 v = __ldcg(reinterpret_cast<const float4*>(p) + 1);
   x[0] = u.x; x[1] = u.y; x[2] = u.z; x[3] = u.w;
   x[4] = v.x; x[5] = v.y; x[6] = v.z; x[7] = v.w;
 }
 template <>
-__device__ __forceinline__ void read_act<__half>(const uint8_t* blk, uint32_t t, float (&x)[8]) {
-  const uint4 u = *reinterpret_cast<const uint4*>(blk + 16 * t);
+__device__ __forceinline__ void load_act<__half>(const __half* p, float (&x)[8]) {
+  const uint4 u = __ldcg(reinterpret_cast<const uint4*>(p));
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
   for (int j = 0; j < 4; j++) {
@@ -217,9 +219,19 @@ __global__ void __launch_bounds__(GEMV_THREADS, 4)
     *reinterpret_cast<uint4*>(smem + off_zero(nb)) = make_uint4(0u, 0u, 0u, 0u);
   __syncthreads();
 
-  // ---- every copy of the tile, in flight at once ----
-  // warp w copies columns w and w + 8: weights and scales one block per lane,
-  // then the words holding the column's zero points
+  // ---- the constant inputs, all in flight at once: group 0 = the zero point
+  // words, group 1 = the weights and scales (warp w: columns w and w + 8, one
+  // block per lane)
+#pragma unroll
+  for (uint32_t h = 0; h < 2; h++) {
+    const uint32_t j = warp + 8 * h;
+    const ColSm cr = cols[j];
+    if (!cr.live) continue;
+    const uint32_t w0 = (cr.c * nb) >> 3, n_w = ((cr.c * nb + nb - 1) >> 3) - w0 + 1;
+    for (uint32_t k = lane; k < n_w; k += 32)
+      cp_async4(sbase + (uint32_t)off_zc(nb) + (j * zc + k) * 4, cr.z + w0 + k);
+  }
+  cp_async_commit();
 #pragma unroll
   for (uint32_t h = 0; h < 2; h++) {
     const uint32_t j = warp + 8 * h;
@@ -231,51 +243,13 @@ __global__ void __launch_bounds__(GEMV_THREADS, 4)
       cp_async16(w_dst + b * 16, cr.w + (size_t)b * 16);
       cp_async4(s_dst + b * 64, cr.s + b);
     }
-    const uint32_t w0 = (cr.c * nb) >> 3, n_w = ((cr.c * nb + nb - 1) >> 3) - w0 + 1;
-    for (uint32_t k = lane; k < n_w; k += 32)
-      cp_async4(sbase + (uint32_t)off_zc(nb) + (j * zc + k) * 4, cr.z + w0 + k);
   }
-  // everything above reads only the weights; the activations (and the outputs)
-  // belong to the kernels around this one
-  nwd::pdl_wait();
-  // the activations: 16-byte pieces of each block's 128-byte slot
-  {
-    constexpr uint32_t PIECES = sizeof(AT) * 32 / 16;  // 8 (f32) or 4 (f16)
-    constexpr uint32_t ELEMS = 16 / sizeof(AT);
-    for (uint32_t i = threadIdx.x; i < nb * PIECES; i += GEMV_THREADS) {
-      const uint32_t b = i / PIECES, piece = i % PIECES;
-      cp_async16(sbase + (uint32_t)off_a(nb) + b * 128 + piece * 16, a + (size_t)i * ELEMS);
-    }
-  }
-  cp_async_wait_all();
-  __syncthreads();
+  cp_async_commit();
 
-  // ---- B fragments in place over the raw activations: lane (block, t) turns
-  // elements [8t, 8t + 8) into uint4 [row][t] of its block; a warp's 8 blocks
-  // per round are its own, so a warp barrier separates the reads and writes
-  for (uint32_t base = warp * 32; base < nb * 4; base += GEMV_THREADS) {
-    const uint32_t item = base + lane, bb = item >> 2, tt = item & 3;
-    const bool on = item < nb * 4;
-    uint8_t* blk = smem + off_a(nb) + (size_t)bb * 128;
-    float x[8];
-    if (on) read_act<AT>(blk, tt, x);
-    __syncwarp();
-    if (on) {
-      __half hi[8], lo[8];
-#pragma unroll
-      for (int j = 0; j < 8; j++) {
-        hi[j] = __float2half_rn(x[j]);
-        lo[j] = __float2half_rn(x[j] - __half2float(hi[j]));
-      }
-      // step s: {(e, e+4), (e+1, e+5)} with e = 2s
-      reinterpret_cast<uint4*>(blk)[tt] = make_uint4(pack_h2(hi[0], hi[4]), pack_h2(hi[1], hi[5]),
-                                                     pack_h2(hi[2], hi[6]), pack_h2(hi[3], hi[7]));
-      reinterpret_cast<uint4*>(blk)[4 + tt] = make_uint4(pack_h2(lo[0], lo[4]), pack_h2(lo[1], lo[5]),
-                                                         pack_h2(lo[2], lo[6]), pack_h2(lo[3], lo[7]));
-    }
-    __syncwarp();
-  }
-  // ---- the zero point table: (block, column) -> fp16 pair (1024 + z, 64 + z)
+  // ---- the zero point table, (block, column) -> fp16 pair (1024 + z, 64 + z),
+  // as soon as the words are in (the weights may still be arriving)
+  cp_async_wait_pending(1);
+  __syncthreads();
   {
     uint32_t* zt = reinterpret_cast<uint32_t*>(smem + off_zt(nb));
     const uint32_t j = threadIdx.x & 15;
@@ -286,6 +260,31 @@ __global__ void __launch_bounds__(GEMV_THREADS, 4)
       zt[(b * 8 + (j & 7)) * 2 + (j >> 3)] = (0x6400u | z) | ((0x5400u | (z << 4)) << 16);
     }
   }
+
+  // everything above reads only the weights; the activations (and the outputs)
+  // belong to the kernels around this one
+  nwd::pdl_wait();
+
+  // ---- B fragments straight from the activations in global memory: thread
+  // (block, t) loads elements [8t, 8t + 8) and writes uint4 [row][t] of its block
+  for (uint32_t item = threadIdx.x; item < nb * 4; item += GEMV_THREADS) {
+    const uint32_t bb = item >> 2, tt = item & 3;
+    float x[8];
+    load_act<AT>(a + (size_t)bb * 32 + tt * 8, x);
+    __half hi[8], lo[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      hi[k] = __float2half_rn(x[k]);
+      lo[k] = __float2half_rn(x[k] - __half2float(hi[k]));
+    }
+    // step s: {(e, e+4), (e+1, e+5)} with e = 2s
+    uint4* blk = reinterpret_cast<uint4*>(smem + off_a(nb) + (size_t)bb * 128);
+    blk[tt] = make_uint4(pack_h2(hi[0], hi[4]), pack_h2(hi[1], hi[5]), pack_h2(hi[2], hi[6]),
+                         pack_h2(hi[3], hi[7]));
+    blk[4 + tt] = make_uint4(pack_h2(lo[0], lo[4]), pack_h2(lo[1], lo[5]), pack_h2(lo[2], lo[6]),
+                             pack_h2(lo[3], lo[7]));
+  }
+  cp_async_wait_pending(0);
   __syncthreads();
 
   // ---- this warp's eighth of the blocks ----
