@@ -151,7 +151,12 @@ def start_clocks(torch, dev, rank):
     if rank != 0:
         return None
     uuid = str(torch.cuda.get_device_properties(dev).uuid)
-    return ClockSampler(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+    sampler = ClockSampler(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+    # short timed regions: have at least the first sample before the warm-up starts
+    t = time.monotonic()
+    while sampler.proc and not sampler.rows and time.monotonic() - t < 5.0:
+        time.sleep(0.05)
+    return sampler
 
 def import_pkg():
     if REPO not in sys.path:
@@ -900,7 +905,8 @@ def run_config6(args, ops, torch, dist, dev, rank, world):
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
                          "frac": gbs / peak, "kernel": "q4_gemv_kernel (q/k/v + append)",
                          "launch_ms": qkv_max, "bytes_per_launch": qkv_bytes,
-                         "traffic": None, "peak_source": f"{kind} (hbm_gbs)"},
+                         "traffic": profiled_traffic("q4_gemv_kernel_config6_traffic"),
+                         "peak_source": f"{kind} (hbm_gbs)"},
             "e2e": ({"value": world * args.steps / (e2e_max * 1e-3), "unit": "tokens/s",
                      "h2d_bytes_per_step": N_ATTN_LAYERS * HIDDEN6 * 4,
                      "d2h_bytes_per_step": HIDDEN6 * 4} if e2e is not None else None),
