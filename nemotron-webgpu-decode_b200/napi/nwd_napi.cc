@@ -10,8 +10,16 @@
 //       kernels/sparse_attn.wgsl Params {n_heads, n_kv_heads, head_dim, seq}
 //   nwd.kvAppendAttention(q, kNew, vNew, kCache, vCache, o, {..., seq, cap})
 //       the engine step of runtime.js:389-391 in one launch
-//   nwd.alloc(bytes) / nwd.free(buf) / nwd.upload(buf, typedArray) / nwd.download(buf, typedArray)
-// Buffers are napi_external wrappers of device pointers.  A non-zero status
+//   nwd.q4Gemv(a, {b, scales, zp}, y, {K, N, n_blocks, epilogue, a_f16})
+//       kernels/matmul_nbits_sg.wgsl Params {K, N, n_blocks, epilogue}
+//       (runtime.js:212-218); the weight object is the engine's q4 buffers;
+//       a_f16 = 1 for an fp16 activation vector (the attention output)
+//   nwd.q4QkvAppend(hNorm, wq, wk, wv, qOut, kCache, vCache,
+//                   {seq, cap, K, n_heads, n_kv_heads, head_dim})
+//       the q/k/v GEMVs and both kv_append dispatches of runtime.js:385-390
+//   nwd.alloc(bytes) / nwd.upload(buf, typedArray) / nwd.download(buf, typedArray)
+// Buffers are napi_external wrappers of device pointers, freed when the
+// wrapper is garbage-collected.  A non-zero status
 // throws Error(nwd_last_error()), as runtime.js throws on errors (:448, :484).
 #include <cuda_runtime.h>
 #include <node_api.h>
@@ -189,6 +197,66 @@ napi_value KvAppendAttention(napi_env env, napi_callback_info info) {
   return st ? throw_status(env, st) : nullptr;
 }
 
+// {b, scales, zp} -> the three device buffers of one q4 matrix
+bool get_q4(napi_env env, napi_value obj, DevBuf** b, DevBuf** s, DevBuf** z) {
+  napi_value v;
+  const char* keys[3] = {"b", "scales", "zp"};
+  DevBuf** outs[3] = {b, s, z};
+  for (int i = 0; i < 3; i++) {
+    if (napi_get_named_property(env, obj, keys[i], &v) != napi_ok) {
+      napi_throw_type_error(env, nullptr, "expected a q4 weight object {b, scales, zp}");
+      return false;
+    }
+    *outs[i] = get_buf(env, v);
+    if (!*outs[i]) return false;
+  }
+  return true;
+}
+
+napi_value Q4Gemv(napi_env env, napi_callback_info info) {
+  size_t argc = 4;
+  napi_value argv[4];
+  napi_get_cb_info(env, info, &argc, argv, nullptr, nullptr);
+  DevBuf *a = get_buf(env, argv[0]), *y = get_buf(env, argv[2]);
+  DevBuf *b = nullptr, *s = nullptr, *z = nullptr;
+  if (!a || !y || !get_q4(env, argv[1], &b, &s, &z)) return nullptr;
+  const uint32_t K = get_u32(env, argv[3], "K"), N = get_u32(env, argv[3], "N"),
+                 nb = get_u32(env, argv[3], "n_blocks"),
+                 ep = get_u32(env, argv[3], "epilogue", 0, false),
+                 f16 = get_u32(env, argv[3], "a_f16", 0, false);
+  int st = f16 ? nwd_q4_gemv_f16a((const uint16_t*)a->ptr, (const uint32_t*)b->ptr,
+                                  (const float*)s->ptr, (const uint32_t*)z->ptr, (float*)y->ptr, K,
+                                  N, nb, ep, nullptr)
+               : nwd_q4_gemv((const float*)a->ptr, (const uint32_t*)b->ptr, (const float*)s->ptr,
+                             (const uint32_t*)z->ptr, (float*)y->ptr, K, N, nb, ep, nullptr);
+  return st ? throw_status(env, st) : nullptr;
+}
+
+napi_value Q4QkvAppend(napi_env env, napi_callback_info info) {
+  size_t argc = 8;
+  napi_value argv[8];
+  napi_get_cb_info(env, info, &argc, argv, nullptr, nullptr);
+  DevBuf *h = get_buf(env, argv[0]), *q = get_buf(env, argv[4]), *kc = get_buf(env, argv[5]),
+         *vc = get_buf(env, argv[6]);
+  DevBuf *bq = nullptr, *sq = nullptr, *zq = nullptr, *bk = nullptr, *sk = nullptr,
+         *zk = nullptr, *bv = nullptr, *sv = nullptr, *zv = nullptr;
+  if (!h || !q || !kc || !vc || !get_q4(env, argv[1], &bq, &sq, &zq) ||
+      !get_q4(env, argv[2], &bk, &sk, &zk) || !get_q4(env, argv[3], &bv, &sv, &zv))
+    return nullptr;
+  const uint32_t nh = get_u32(env, argv[7], "n_heads"), nkv = get_u32(env, argv[7], "n_kv_heads"),
+                 hd = get_u32(env, argv[7], "head_dim"), seq = get_u32(env, argv[7], "seq"),
+                 K = get_u32(env, argv[7], "K");
+  const uint32_t cap =
+      get_u32(env, argv[7], "cap", (uint32_t)(kc->bytes / (2ull * nkv * hd)), false);
+  int st = nwd_q4_qkv_append(
+      (const float*)h->ptr, (const uint32_t*)bq->ptr, (const float*)sq->ptr,
+      (const uint32_t*)zq->ptr, (const uint32_t*)bk->ptr, (const float*)sk->ptr,
+      (const uint32_t*)zk->ptr, (const uint32_t*)bv->ptr, (const float*)sv->ptr,
+      (const uint32_t*)zv->ptr, (uint16_t*)q->ptr, (uint16_t*)kc->ptr, (uint16_t*)vc->ptr, seq,
+      cap, K, nh, nkv, hd, nullptr);
+  return st ? throw_status(env, st) : nullptr;
+}
+
 napi_value Init(napi_env env, napi_value exports) {
   napi_property_descriptor props[] = {
       {"alloc", nullptr, Alloc, nullptr, nullptr, nullptr, napi_default, nullptr},
@@ -198,6 +266,8 @@ napi_value Init(napi_env env, napi_value exports) {
       {"attention", nullptr, Attention, nullptr, nullptr, nullptr, napi_default, nullptr},
       {"kvAppendAttention", nullptr, KvAppendAttention, nullptr, nullptr, nullptr, napi_default,
        nullptr},
+      {"q4Gemv", nullptr, Q4Gemv, nullptr, nullptr, nullptr, napi_default, nullptr},
+      {"q4QkvAppend", nullptr, Q4QkvAppend, nullptr, nullptr, nullptr, napi_default, nullptr},
   };
   napi_define_properties(env, exports, sizeof(props) / sizeof(props[0]), props);
   return exports;
