@@ -551,8 +551,21 @@ def run_small_configs(args, ops, torch, dev, rank, world):
     nh = 40
     out = []
 
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def replay_ms(g, reps, stream):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            g.replay()
+        b.record(stream)
+        b.synchronize()
+        return a.elapsed_time(b)
+
     def timed_graph(layer, seqs, q, kn, o):
-        """Capture one fused step per entry of `seqs`; return (ms per step, bytes per step)."""
+        """Capture one fused step per entry of `seqs`, each after an L2 flush (a write
+        larger than L2), and the same flushes alone; return (ms per step, bytes per
+        step, steps): the step's time is replay(flush + step) - replay(flush)."""
         stream = torch.cuda.Stream()
         nbytes = sum(4096 * (x + 1) + 2 * nh * HD * 2 + 4 * HKV * HD * 2 for x in seqs) / len(seqs)
         with torch.cuda.stream(stream):
@@ -562,27 +575,34 @@ def run_small_configs(args, ops, torch, dev, rank, world):
             stream.synchronize()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
-                for x in seqs:
+                for i, x in enumerate(seqs):
+                    flush.fill_(i & 0xFF)
                     layer.seq = x
                     layer.step(q, kn, kn, out=o)
-            reps = max(1, args.steps // len(seqs))
+            gf = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gf, stream=stream):
+                for i in range(len(seqs)):
+                    flush.fill_(i & 0xFF)
+            reps = max(5, args.steps // len(seqs))
             for _ in range(max(1, args.warmup // len(seqs)) + 2):
                 g.replay()
+                gf.replay()
             stream.synchronize()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
+            # interleaved, so clock drift hits both alike
+            t_both = t_flush = 0.0
             for _ in range(reps):
-                g.replay()
-            b.record(stream)
-            b.synchronize()
-        ms = a.elapsed_time(b) / (reps * len(seqs))
-        del g
+                t_both += replay_ms(g, 1, stream)
+                t_flush += replay_ms(gf, 1, stream)
+        ms = (t_both - t_flush) / (reps * len(seqs))
+        del g, gf
         return ms, nbytes, reps * len(seqs)
 
     def line(workload, ms, nbytes, steps, extra):
         gbs = nbytes / (ms * 1e-3) / 1e9
         cfg = {"workload": workload, "heads": nh, "kv_heads": HKV, "head_dim": HD,
-               "launches_per_step": 1, "timing": "CUDA graph replay of the step sequence"}
+               "launches_per_step": 1, "timing": "CUDA graph replay of the step sequence",
+               "l2": f"flushed before every step ({FLUSH_BYTES >> 20} MB write); step time = "
+                     "replay(flush + step) - replay(flush)"}
         cfg.update(extra)
         return {"metric": METRIC, "value": 1e3 / ms, "unit": "tokens/s", "n_gpus": 1,
                 "steps": steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -591,6 +611,8 @@ def run_small_configs(args, ops, torch, dev, rank, world):
                 "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
                              "frac": gbs / peak}}
 
+    sampler = start_clocks(torch, dev, rank)
+    t0 = time.monotonic()
     if args.config == "1":
         layer = engine.DecodeAttention(nh, HKV, HD, 256)
         ops.fill_normal(layer.k_cache, 11)
@@ -612,6 +634,12 @@ def run_small_configs(args, ops, torch, dev, rank, world):
             ms, nbytes, steps = timed_graph(layer, [L - 1 + j for j in range(POS_CYCLE)], q, kn, o)
             out.append(line(f"config2-L{L}", ms, nbytes, steps, {"kv_len": L}))
             del layer
+    t1 = time.monotonic()
+    if sampler:
+        sampler.stop()
+        clocks = sampler.summary(t0, t1)
+        for ln in out:
+            ln["clocks"] = clocks
     for ln in out:
         print(json.dumps(ln), flush=True)
     return 0
@@ -737,6 +765,7 @@ HIDDEN6, HQ6 = 3136, 40          # engine/config.js: hidden, heads
 N_ATTN_LAYERS = 4                 # engine/config.js ATTN_LAYERS
 L6 = 150                          # rows already cached (config 1's trace end)
 WEIGHT_SETS = 3                   # rotating copies: 3 x 99 MB of q4 weights > L2
+FLUSH_BYTES = 192 << 20           # configs 1 / 2: a write this large evicts L2 (126 MB) before each step
 
 
 def _q4_random(ops, torch, n, n_blocks, gen, dev):
