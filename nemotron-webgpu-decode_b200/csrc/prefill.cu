@@ -20,16 +20,15 @@
 //               shared-memory descriptors.
 //   warp 1      MMA issuer (one thread).  Over the flattened sequence of
 //               blocks g of all its tiles: S(g) = Q K(g)^T into TMEM score
-//               buffer g & 1 (M=128 queries, N=128 keys, K=128 = 8 MMAs of
-//               K=16), up to one block ahead so it overlaps the softmax of
-//               block g-1; then, once P(g) is in TMEM, O += P V into the
-//               tile's TMEM accumulator (two, alternating by tile) with A = P
-//               read from tensor memory and B = V an MN-major shared-memory
-//               operand.  P is an fp16 head and an fp16 remainder (16 MMAs):
+//               buffer g mod 3 (M=128 queries, N=128 keys, K=128 = 8 MMAs of
+//               K=16), up to two blocks ahead of the P V MMAs so the softmax
+//               never waits for them; then, once P(g) is in TMEM, O += P V
+//               into the TMEM accumulator with A = P read from tensor memory
+//               and B = V an MN-major shared-memory operand.  P is an fp16 head and an fp16 remainder (16 MMAs):
 //               one fp16 rounding of P would exceed the parity tolerance on
 //               outputs near zero.  tcgen05.commit signals S ready, K/V/Q
 //               free, PV done and O complete.
-//   warp 2      TMEM allocation (512 columns: S0, S1, O0, O1) and release.
+//   warp 2      TMEM allocation (512 columns: S0, S1, S2, O) and release.
 //   warps 4-7   softmax: thread r owns query row r (TMEM lane r).  Per block
 //               it reads its 128 scores (240 registers per thread: the other
 //               warpgroups give theirs up with setmaxnreg), applies the causal
@@ -37,13 +36,13 @@
 //               rescaled in TMEM only when a row's max grows by more than
 //               2^8), and writes P = 2^(s - m) over its own scores as fp16
 //               pairs (per half: head, then remainder).  P(g) needs no wait on
-//               PV(g-1), which reads the other buffer; the MMAs of one thread
-//               run in issue order, so S(g+2) overwrites P(g) only after
+//               PV(g-1), which reads another buffer; the MMAs of one thread
+//               run in issue order, so S(g+3) overwrites P(g) only after
 //               PV(g) has read it.  At the end of a tile it hands the row sums
 //               to the epilogue through shared memory.
 //   warps 8-11  epilogue: per tile, once its last PV has completed, divides
 //               O by the row sum and stores it as fp16, then frees the O
-//               buffer for the tile after next.
+//               accumulator for the next tile's first PV.
 // K/V rows past the chunk's end that a block covers are zeroed in shared
 // memory before P V reads them (P is 0 there, but 0 x NaN would not be).
 // All waits are bounded; on expiry the kernel records
