@@ -804,6 +804,7 @@ struct Tuning {
   uint32_t pair_max = 512;
   uint32_t groups = 0;  // consumer groups: 0 = by problem size, else 1 or 2
   uint32_t two_group_rows = 8192;  // single sequence: two groups from this many rows
+  uint32_t short_rows = 256;  // single sequence of at most this many rows: decode_short.cu
 };
 
 uint32_t env_u32(const char* name, uint32_t dflt) {
@@ -821,6 +822,10 @@ const Tuning& tuning() {
     x.groups = env_u32("NWD_DECODE_GROUPS", x.groups);
     if (x.groups > 2) x.groups = 2;
     x.two_group_rows = env_u32("NWD_DECODE_TWO_GROUP_ROWS", x.two_group_rows);
+    // 0 turns the short-sequence kernel off
+    const char* sr = getenv("NWD_DECODE_SHORT_ROWS");
+    if (sr && *sr) x.short_rows = (uint32_t)strtoul(sr, nullptr, 10);
+    if (x.short_rows > nwd::decode_short_max_rows()) x.short_rows = nwd::decode_short_max_rows();
     return x;
   }();
   return t;
@@ -897,6 +902,17 @@ int launch(const Call& c) {
   if ((uintptr_t)c.ws & 255u)
     return fail(NWD_ERR_WORKSPACE, "%s: workspace must be 256-byte aligned", c.who);
   if (c.batch == 0) return ok();
+  if (!(c.scale >= 0.f) || isinf(c.scale))
+    return fail(NWD_ERR_INVALID, "%s: scale must be finite and >= 0 (0 = 1/sqrt(head_dim))", c.who);
+
+  // one short sequence: the single-CTA-per-kv-head kernel (no workspace use)
+  if (!c.seq_len && !c.partial && c.single_len >= 1 &&
+      (uint32_t)c.single_len <= tu.short_rows) {
+    const float sc = c.scale != 0.f ? c.scale : 1.0f / sqrtf((float)c.hd);
+    return launch_decode_short(c.q, c.k_new, c.v_new, const_cast<uint16_t*>(c.k_pool),
+                               const_cast<uint16_t*>(c.v_pool), c.o, (uint32_t)c.single_len,
+                               c.n_kv, G, sc * 1.4426950408889634f, c.append, c.stream, c.who);
+  }
 
   CUtensorMap tmk, tmv;
   st = kv_tensor_map(&tmk, c.k_pool, c.pool_rows, c.n_kv, c.hd, TOK);

@@ -48,9 +48,18 @@ def test_group_sizes(ops, oracle, nh, nkv):
     assert_attn_close(got, ref, f"Hq={nh} Hkv={nkv}")
 
 
-def test_custom_scale(ops, oracle):
-    got, ref = _single(ops, oracle, 32, 8, 500, 512, seed=5, scale=0.03)
-    assert_attn_close(got, ref, "scale=0.03")
+@pytest.mark.parametrize("nh,nkv,L", [(8, 8, 151), (16, 8, 33), (24, 8, 151), (56, 8, 200),
+                                      (64, 8, 256), (16, 2, 97), (5, 1, 151), (3, 1, 1)])
+def test_group_sizes_short(ops, oracle, nh, nkv, L):
+    """Every group size (1..8) on the single-CTA-per-kv-head kernel (<= 256 rows)."""
+    got, ref = _single(ops, oracle, nh, nkv, L, L + 5, seed=41 + L)
+    assert_attn_close(got, ref, f"Hq={nh} Hkv={nkv} L={L}")
+
+
+@pytest.mark.parametrize("L", [200, 500])
+def test_custom_scale(ops, oracle, L):
+    got, ref = _single(ops, oracle, 32, 8, L, 512, seed=5, scale=0.03)
+    assert_attn_close(got, ref, f"scale=0.03 L={L}")
 
 
 def test_zero_length_writes_zeros(ops):
