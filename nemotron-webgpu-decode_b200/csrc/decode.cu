@@ -804,7 +804,8 @@ struct Tuning {
   uint32_t pair_max = 512;
   uint32_t groups = 0;  // consumer groups: 0 = by problem size, else 1 or 2
   uint32_t two_group_rows = 8192;  // single sequence: two groups from this many rows
-  uint32_t short_rows = 256;  // single sequence of at most this many rows: decode_short.cu
+  uint32_t short_rows = 2048;  // single sequence of at most this many rows: decode_short.cu
+  uint32_t short_cta_rows = 128;  // past 256 rows: rows per CTA of a kv head's cluster
 };
 
 uint32_t env_u32(const char* name, uint32_t dflt) {
@@ -826,6 +827,7 @@ const Tuning& tuning() {
     const char* sr = getenv("NWD_DECODE_SHORT_ROWS");
     if (sr && *sr) x.short_rows = (uint32_t)strtoul(sr, nullptr, 10);
     if (x.short_rows > nwd::decode_short_max_rows()) x.short_rows = nwd::decode_short_max_rows();
+    x.short_cta_rows = env_u32("NWD_DECODE_SHORT_CTA_ROWS", x.short_cta_rows);
     return x;
   }();
   return t;
@@ -905,13 +907,14 @@ int launch(const Call& c) {
   if (!(c.scale >= 0.f) || isinf(c.scale))
     return fail(NWD_ERR_INVALID, "%s: scale must be finite and >= 0 (0 = 1/sqrt(head_dim))", c.who);
 
-  // one short sequence: the single-CTA-per-kv-head kernel (no workspace use)
+  // one short sequence: a cluster of CTAs per kv head (no workspace use)
   if (!c.seq_len && !c.partial && c.single_len >= 1 &&
       (uint32_t)c.single_len <= tu.short_rows) {
     const float sc = c.scale != 0.f ? c.scale : 1.0f / sqrtf((float)c.hd);
     return launch_decode_short(c.q, c.k_new, c.v_new, const_cast<uint16_t*>(c.k_pool),
                                const_cast<uint16_t*>(c.v_pool), c.o, (uint32_t)c.single_len,
-                               c.n_kv, G, sc * 1.4426950408889634f, c.append, c.stream, c.who);
+                               c.n_kv, G, sc * 1.4426950408889634f, c.append, tu.short_cta_rows,
+                               c.stream, c.who);
   }
 
   CUtensorMap tmk, tmv;

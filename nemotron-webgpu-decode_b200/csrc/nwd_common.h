@@ -36,14 +36,15 @@ int kv_tensor_map(CUtensorMap* out, const void* base, uint64_t rows, uint32_t n_
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // ---- decode of one short sequence (decode_short.cu) ----
-// One CTA per kv head, K and V staged in shared memory: for 1..max rows and
-// at most 8 query heads per kv head, head_dim 128.  With append, row L - 1
-// comes from k_new / v_new and is written to the caches.
+// A cluster of CTAs per kv head, each holding about cta_rows of its K and V
+// rows in shared memory (0 = the most a CTA holds): for 1..max rows and at
+// most 8 query heads per kv head, head_dim 128.  With append, row L - 1 comes
+// from k_new / v_new and is written to the caches.
 uint32_t decode_short_max_rows();
 int launch_decode_short(const uint16_t* q, const uint16_t* k_new, const uint16_t* v_new,
                         uint16_t* k_cache, uint16_t* v_cache, uint16_t* o, uint32_t L,
                         uint32_t n_kv, uint32_t group, float scale_log2, bool append,
-                        void* stream, const char* who);
+                        uint32_t cta_rows, void* stream, const char* who);
 
 // ---- programmatic dependent launch ----
 // A kernel launched with launch_pdl() may start while the kernel before it in
