@@ -167,6 +167,28 @@ def test_engine_trace_config1(engine_mod, oracle):
     assert layer.workspace.check() == 0
 
 
+@pytest.mark.parametrize("seq", [0, 255, 256, 700, 2047, 2100])
+def test_fused_append_single(ops, oracle, seq):
+    """kv_append + attention in one call at the one-CTA, cluster and general
+    kernels' row counts (seq + 1 rows): the new row lands in the caches and in
+    the output; every other cache row is untouched."""
+    nh, nkv, hd, cap = 40, 8, 128, seq + 9
+    q = oracle.normal_f16(nh * hd, 51)
+    kn = oracle.normal_f16(nkv * hd, 52)
+    vn = oracle.normal_f16(nkv * hd, 53)
+    kc = oracle.normal_f16(cap * nkv * hd, 54).reshape(cap, nkv, hd)
+    vc = oracle.normal_f16(cap * nkv * hd, 55).reshape(cap, nkv, hd)
+    dk, dv = to_dev(kc), to_dev(vc)
+    o = torch.empty(nh, hd, dtype=torch.float16, device="cuda")
+    ops.kv_append_attention(to_dev(q, (nh, hd)), to_dev(kn, (nkv, hd)), to_dev(vn, (nkv, hd)),
+                            dk, dv, o, ops.AttnParams(nh, nkv, hd, seq))
+    oracle.kv_append(kn, kc, seq, nkv, hd)
+    oracle.kv_append(vn, vc, seq, nkv, hd)
+    ref = oracle.attention(q, kc, vc, nh, nkv, hd, seq + 1)
+    assert_attn_close(vals(o), ref, f"fused append at row {seq}")
+    assert np.array_equal(bits(dk), kc) and np.array_equal(bits(dv), vc)
+
+
 def test_engine_prompt_chunk_then_steps(engine_mod, oracle):
     """BASELINE config 1 with the 24-token prompt as one chunk (DecodeAttention.prefill,
     the tcgen05 kernel) instead of 24 steps, then 127 decode steps: every output matches
