@@ -266,23 +266,33 @@ __global__ void __launch_bounds__(GEMV_THREADS, 4)
   nwd::pdl_wait();
 
   // ---- B fragments straight from the activations in global memory: thread
-  // (block, t) loads elements [8t, 8t + 8) and writes uint4 [row][t] of its block
-  for (uint32_t item = threadIdx.x; item < nb * 4; item += GEMV_THREADS) {
-    const uint32_t bb = item >> 2, tt = item & 3;
-    float x[8];
-    load_act<AT>(a + (size_t)bb * 32 + tt * 8, x);
-    __half hi[8], lo[8];
+  // (block, t) loads elements [8t, 8t + 8) and writes uint4 [row][t] of its
+  // block; two items' loads are in flight before either is converted
+  for (uint32_t item = threadIdx.x; item < nb * 4; item += 2 * GEMV_THREADS) {
+    float x[2][8];
+    const bool second = item + GEMV_THREADS < nb * 4;
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-      hi[k] = __float2half_rn(x[k]);
-      lo[k] = __float2half_rn(x[k] - __half2float(hi[k]));
+    for (uint32_t u = 0; u < 2; u++) {
+      const uint32_t it = item + u * GEMV_THREADS;
+      if (u == 0 || second) load_act<AT>(a + (size_t)(it >> 2) * 32 + (it & 3) * 8, x[u]);
     }
-    // step s: {(e, e+4), (e+1, e+5)} with e = 2s
-    uint4* blk = reinterpret_cast<uint4*>(smem + off_a(nb) + (size_t)bb * 128);
-    blk[tt] = make_uint4(pack_h2(hi[0], hi[4]), pack_h2(hi[1], hi[5]), pack_h2(hi[2], hi[6]),
-                         pack_h2(hi[3], hi[7]));
-    blk[4 + tt] = make_uint4(pack_h2(lo[0], lo[4]), pack_h2(lo[1], lo[5]), pack_h2(lo[2], lo[6]),
-                             pack_h2(lo[3], lo[7]));
+#pragma unroll
+    for (uint32_t u = 0; u < 2; u++) {
+      if (u == 1 && !second) break;
+      const uint32_t it = item + u * GEMV_THREADS, bb = it >> 2, tt = it & 3;
+      __half hi[8], lo[8];
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        hi[k] = __float2half_rn(x[u][k]);
+        lo[k] = __float2half_rn(x[u][k] - __half2float(hi[k]));
+      }
+      // step s: {(e, e+4), (e+1, e+5)} with e = 2s
+      uint4* blk = reinterpret_cast<uint4*>(smem + off_a(nb) + (size_t)bb * 128);
+      blk[tt] = make_uint4(pack_h2(hi[0], hi[4]), pack_h2(hi[1], hi[5]), pack_h2(hi[2], hi[6]),
+                           pack_h2(hi[3], hi[7]));
+      blk[4 + tt] = make_uint4(pack_h2(lo[0], lo[4]), pack_h2(lo[1], lo[5]), pack_h2(lo[2], lo[6]),
+                               pack_h2(lo[3], lo[7]));
+    }
   }
   cp_async_wait_pending(0);
   __syncthreads();
@@ -297,7 +307,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 4)
   const uint32_t fstride = lane < 8 ? 128u : 0u;
   float accH0 = 0.f, accL0 = 0.f, accH1 = 0.f, accL1 = 0.f;  // columns g and g + 8
   const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 2
+  // the two K-steps of a block are independent MMAs (no accumulate chain
+  // between them), so several blocks' MMAs are in flight at once
+#pragma unroll 4
   for (uint32_t b = b_lo; b < b_hi; b++) {
     const uint32_t x0 = ws[(g * cs + b) * 4 + t];
     const uint32_t x1 = ws[((g + 8) * cs + b) * 4 + t];
@@ -307,21 +319,21 @@ __global__ void __launch_bounds__(GEMV_THREADS, 4)
     const __half2 zl0 = __low2half2(bits_h2(zu.x)), zh0 = __high2half2(bits_h2(zu.x));
     const __half2 zl1 = __low2half2(bits_h2(zu.y)), zh1 = __high2half2(bits_h2(zu.y));
     const uint32_t x0s = x0 >> 8, x1s = x1 >> 8;
-    float d[4];
+    float d[4], e[4];
     mma16816(d, h2_bits(__hsub2(bits_h2(lop3_or_and(x0, 0x000F000Fu, 0x64006400u)), zl0)),
              h2_bits(__hsub2(bits_h2(lop3_or_and(x1, 0x000F000Fu, 0x64006400u)), zl1)),
              h2_bits(__hsub2(bits_h2(lop3_or_and(x0, 0x00F000F0u, 0x54005400u)), zh0)),
              h2_bits(__hsub2(bits_h2(lop3_or_and(x1, 0x00F000F0u, 0x54005400u)), zh1)), f.x, f.y,
              zero4);
-    mma16816(d, h2_bits(__hsub2(bits_h2(lop3_or_and(x0s, 0x000F000Fu, 0x64006400u)), zl0)),
+    mma16816(e, h2_bits(__hsub2(bits_h2(lop3_or_and(x0s, 0x000F000Fu, 0x64006400u)), zl0)),
              h2_bits(__hsub2(bits_h2(lop3_or_and(x1s, 0x000F000Fu, 0x64006400u)), zl1)),
              h2_bits(__hsub2(bits_h2(lop3_or_and(x0s, 0x00F000F0u, 0x54005400u)), zh0)),
              h2_bits(__hsub2(bits_h2(lop3_or_and(x1s, 0x00F000F0u, 0x54005400u)), zh1)), f.z, f.w,
-             d);
-    accH0 = fmaf(sc.x, d[0], accH0);
-    accL0 = fmaf(sc.x, d[1], accL0);
-    accH1 = fmaf(sc.y, d[2], accH1);
-    accL1 = fmaf(sc.y, d[3], accL1);
+             zero4);
+    accH0 = fmaf(sc.x, d[0] + e[0], accH0);
+    accL0 = fmaf(sc.x, d[1] + e[1], accL0);
+    accH1 = fmaf(sc.y, d[2] + e[2], accH1);
+    accL1 = fmaf(sc.y, d[3] + e[3], accL1);
   }
   // lanes t == 0 hold columns g and g + 8 (D columns 0 and 1; the rest are zero)
   if (t == 0) {
