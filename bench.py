@@ -597,6 +597,32 @@ def run_small_configs(args, ops, torch, dev, rank, world):
         del g, gf
         return ms, nbytes, reps * len(seqs)
 
+    def timed_graph_rotating(layers, seqs, q, kn, o):
+        """One fused step per (position, sequence), the sequences visited in turn;
+        return (ms per step, bytes per step, steps)."""
+        stream = torch.cuda.Stream()
+        nbytes = sum(4096 * (x + 1) + 2 * nh * HD * 2 + 4 * HKV * HD * 2 for x in seqs) / len(seqs)
+        n = len(seqs) * len(layers)
+        with torch.cuda.stream(stream):
+            for x in seqs:  # warm (and first-call set-up) outside the capture
+                for layer in layers:
+                    layer.seq = x
+                    layer.step(q, kn, kn, out=o)
+            stream.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for x in seqs:
+                    for layer in layers:
+                        layer.seq = x
+                        layer.step(q, kn, kn, out=o)
+            reps = max(3, args.steps // n)
+            for _ in range(max(1, args.warmup // n) + 2):
+                g.replay()
+            stream.synchronize()
+            t = replay_ms(g, reps, stream)
+        del g
+        return t / (reps * n), nbytes, reps * n
+
     def line(workload, ms, nbytes, steps, extra):
         gbs = nbytes / (ms * 1e-3) / 1e9
         cfg = {"workload": workload, "heads": nh, "kv_heads": HKV, "head_dim": HD,
@@ -625,15 +651,24 @@ def run_small_configs(args, ops, torch, dev, rank, world):
                         {"kv_len": "1..151 (24 prompt + 127 decode steps)"}))
     else:
         for L in ([args.kv_len] if args.kv_len else (1024, 4096, 16384, 32768)):
-            layer = engine.DecodeAttention(nh, HKV, HD, L + POS_CYCLE)
-            ops.fill_normal(layer.k_cache, 21)
-            ops.fill_normal(layer.v_cache, 22)
+            # independent sequences whose caches together exceed L2 by far, visited in
+            # turn: every step reads its K/V cold (and L2 holds no dirty lines to write back)
+            copies = max(2, -(-ROTATE_BYTES // (L * 4096)))
+            layers = []
+            for c in range(copies):
+                layer = engine.DecodeAttention(nh, HKV, HD, L + POS_CYCLE)
+                ops.fill_normal(layer.k_cache, 21 + 2 * c)
+                ops.fill_normal(layer.v_cache, 22 + 2 * c)
+                layers.append(layer)
             q = ops.fill_normal(torch.empty(nh, HD, dtype=torch.float16, device=dev), 23)
             kn = ops.fill_normal(torch.empty(HKV, HD, dtype=torch.float16, device=dev), 24)
             o = torch.empty(nh, HD, dtype=torch.float16, device=dev)
-            ms, nbytes, steps = timed_graph(layer, [L - 1 + j for j in range(POS_CYCLE)], q, kn, o)
-            out.append(line(f"config2-L{L}", ms, nbytes, steps, {"kv_len": L}))
-            del layer
+            ms, nbytes, steps = timed_graph_rotating(layers, [L - 1 + j for j in range(POS_CYCLE)],
+                                                     q, kn, o)
+            out.append(line(f"config2-L{L}", ms, nbytes, steps,
+                            {"kv_len": L, "l2": f"{copies} sequences visited in turn "
+                             f"({copies * L * 4096 >> 20} MB of K/V > L2); no flush"}))
+            del layers
     t1 = time.monotonic()
     if sampler:
         sampler.stop()
@@ -765,7 +800,8 @@ HIDDEN6, HQ6 = 3136, 40          # engine/config.js: hidden, heads
 N_ATTN_LAYERS = 4                 # engine/config.js ATTN_LAYERS
 L6 = 150                          # rows already cached (config 1's trace end)
 WEIGHT_SETS = 3                   # rotating copies: 3 x 99 MB of q4 weights > L2
-FLUSH_BYTES = 192 << 20           # configs 1 / 2: a write this large evicts L2 (126 MB) before each step
+FLUSH_BYTES = 192 << 20           # config 1: a write this large evicts L2 (126 MB) before each step
+ROTATE_BYTES = 320 << 20          # config 2: K/V of the sequences visited in turn
 
 
 def _q4_random(ops, torch, n, n_blocks, gen, dev):
