@@ -5,10 +5,10 @@
 // TMA pipeline, split partials, merge tickets) is pure latency.
 //
 // A thread-block cluster of C CTAs per kv head (C up to 8, about 64 rows
-// each), 4 warps per CTA.  A CTA copies its share of the head's K and V rows
+// each), 8 warps per CTA.  A CTA copies its share of the head's K and V rows
 // into shared memory with cp.async (16-byte pieces, XOR-swizzled per row so
 // the matrix loads below hit distinct banks), then each warp takes every
-// fourth group of 16 of those keys:
+// eighth group of 16 of those keys:
 //   S = q K^T on mma.sync m16n8k16 (f16 in, f32 accumulate): A = q, the
 //   group's query heads in rows 0-7 (the group is at most 8), B = K rows
 //   loaded with ldmatrix; two 8-key tiles per group.
@@ -17,7 +17,7 @@
 //   tolerance on outputs near zero).  The MMA's A operand takes the heads in
 //   rows 0-7 and the remainders in rows 8-15, so one P V MMA per 8 output
 //   columns carries both; B = V rows through ldmatrix.trans.
-// The four warps' (max, sum, output) meet in shared memory, then the C CTAs'
+// The eight warps' (max, sum, output) meet in shared memory, then the C CTAs'
 // through distributed shared memory (each CTA reads the others' partials
 // after a cluster barrier), in a fixed order.
 // With kv_append fused (runtime.js:389-391 as one call) the new row comes
@@ -29,7 +29,7 @@
 namespace {
 
 constexpr int SHD = 128;        // head_dim
-constexpr int SWARPS = 4;
+constexpr int SWARPS = 8;
 constexpr int STHREADS = SWARPS * 32;
 constexpr int SGMAX = 8;        // query heads per kv head (rows 0-7 of the MMA)
 constexpr uint32_t CTA_ROWS = 256;    // K and V rows one CTA holds in shared memory
