@@ -1,0 +1,72 @@
+"""Host-side pieces of bench.py that decide what a bench line reports (no GPU):
+the clock record taken during the timed region (which throttle reasons make a
+run invalid) and the committed DRAM-traffic figures the roofline quotes."""
+from __future__ import annotations
+
+import importlib.util
+import os
+
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def bench():
+    spec = importlib.util.spec_from_file_location("bench_under_test", os.path.join(REPO, "bench.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _sampler(bench, rows):
+    s = bench.ClockSampler.__new__(bench.ClockSampler)  # no nvidia-smi process
+    s.rows = rows
+    s.proc = None
+    return s
+
+
+def _row(sm, mx=1965, power=600.0, hw="Not Active", hw_th="Not Active", sw_th="Not Active",
+         pcap="Not Active"):
+    # clocks.sm, clocks.max.sm, power.draw, event_reasons.active, then the four named reasons
+    return [str(sm), str(mx), str(power), "0x0", hw, hw_th, sw_th, pcap]
+
+
+def test_clock_summary_inside_timed_window(bench):
+    rows = [(0.5, _row(1000)), (1.0, _row(1900)), (1.2, _row(1950)), (1.4, _row(1965)),
+            (3.0, _row(800, hw="Active"))]
+    c = _sampler(bench, rows).summary(1.0, 2.0)
+    assert c["window"] == "timed" and c["samples"] == 3
+    assert c["sm_mhz"] == 1950.0 and c["sm_max_mhz"] == 1965.0
+    # a slowdown outside the timed region does not count against the run
+    assert c["reasons"] == []
+
+
+def test_clock_summary_reports_throttle_reasons(bench):
+    rows = [(1.0, _row(1400, pcap="Active")), (1.1, _row(1350, sw_th="Active")),
+            (1.2, _row(1300, hw="Active", hw_th="Active"))]
+    c = _sampler(bench, rows).summary(0.0, 2.0)
+    assert c["reasons"] == ["hw_slowdown", "hw_thermal_slowdown", "sw_power_cap",
+                            "sw_thermal_slowdown"]
+
+
+def test_clock_summary_short_region_falls_back_to_all_samples(bench):
+    rows = [(0.1, _row(1965)), (0.3, _row(1965, pcap="Active")), (5.0, _row(1965))]
+    c = _sampler(bench, rows).summary(1.0, 1.01)
+    assert c["window"] == "ramp+warmup+timed" and c["samples"] == 3
+    assert c["reasons"] == ["sw_power_cap"]
+
+
+def test_clock_summary_without_nvidia_smi(bench):
+    c = _sampler(bench, []).summary(0.0, 1.0)
+    assert c["samples"] == 0 and c["sm_mhz"] is None and "unavailable" in c["note"]
+
+
+@pytest.mark.parametrize("name", ["decode_kernel_config3_traffic", "q4_gemv_kernel_config6_traffic"])
+def test_profiled_traffic_files(bench, name):
+    v = bench.profiled_traffic(name)
+    assert v is not None and v > 0
+
+
+def test_profiled_traffic_missing_file(bench):
+    assert bench.profiled_traffic("no_such_profile") is None
