@@ -284,7 +284,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 4)
 #pragma unroll
       for (int k = 0; k < 8; k++) {
         hi[k] = __float2half_rn(x[u][k]);
-        lo[k] = __float2half_rn(x[u][k] - __half2float(hi[k]));
+        // fp16 activations are exact in the head: the remainder row is zero
+        lo[k] = sizeof(AT) == 2 ? __float2half_rn(0.f) : __float2half_rn(x[u][k] - __half2float(hi[k]));
       }
       // step s: {(e, e+4), (e+1, e+5)} with e = 2s
       uint4* blk = reinterpret_cast<uint4*>(smem + off_a(nb) + (size_t)bb * 128);
