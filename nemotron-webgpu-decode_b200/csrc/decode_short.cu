@@ -1,11 +1,12 @@
 // Decode attention for one short sequence (at most SHORT_ROWS cached rows):
 // the engine's own case (kernels/sparse_attn.wgsl:32-113 dispatched once per
 // token by engine/runtime.js:389-391, caches of maxSeq = 256 rows), where the
-// work is a few hundred KB and the general split-KV kernel's machinery (plan,
-// TMA pipeline, split partials, merge tickets) is pure latency.
+// work is at most a few MB and the general split-KV kernel's machinery (plan,
+// TMA pipeline, split partials, merge tickets) is mostly latency.
 //
-// A thread-block cluster of C CTAs per kv head (C up to 8, about 64 rows
-// each), 8 warps per CTA.  A CTA copies its share of the head's K and V rows
+// Up to CTA_ROWS rows a kv head is one CTA, launched without a cluster;
+// beyond, a thread-block cluster of C CTAs (C up to 8, about 128 rows each by
+// default).  8 warps per CTA.  A CTA copies its share of the head's K and V rows
 // into shared memory with cp.async (16-byte pieces, XOR-swizzled per row so
 // the matrix loads below hit distinct banks), then each warp takes every
 // eighth group of 16 of those keys:
