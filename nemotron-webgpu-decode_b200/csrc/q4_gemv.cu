@@ -39,8 +39,8 @@
 // the wait they load the activations (through L2) and write the B fragments
 // into shared memory, then wait for the weights; the 8 warps split the blocks
 // (K) in eighths, and the loop body is shared-memory loads, the nibble
-// unpacking, two independent MMAs (one per K-step) and four add + FMA pairs.  The 8 warps' sums meet in shared memory
-// in a fixed order (deterministic).
+// unpacking, two independent MMAs (one per K-step) and four add + FMA pairs.
+// The 8 warps' sums meet in shared memory in a fixed order (deterministic).
 #include <cuda_fp16.h>
 
 #include <algorithm>
