@@ -261,12 +261,18 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
   const uint32_t B = p.seq_len ? p.batch : 1u;
   const uint32_t G = p.group;
   // launched as a programmatic dependent launch: let the next kernel start
-  // early, and wait for the previous one before touching any memory
+  // early, and wait for the previous one before touching any memory.  A
+  // single sequence's plan reads only the parameters, so it (with the barrier
+  // set-up and the tensor-map prefetch) runs while the previous kernel drains;
+  // a batch's plan reads seq_len, which the previous kernel may write.
   nwd::pdl_trigger();
-  nwd::pdl_wait();
+  const bool early_plan = p.seq_len == nullptr;
+  if (!early_plan) nwd::pdl_wait();
 
   // ---- plan: row prefix S over sequences (S[b] = rows before b) ----
   if (tid == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
     misc->abort = 0;
     misc->last = 0;
     misc->total_rows = 0;
@@ -297,6 +303,7 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
   uint32_t run = block_scan<NTHR>((uint32_t)rows_local, misc, &total32);  // syncs: sums final
   if (misc->total_rows >= (1ull << 32)) {
     // more than 2^32 rows in one call: refuse (uniform across the block)
+    if (early_plan) nwd::pdl_wait();
     if (tid == 0 && blockIdx.x == 0) atomicOr(&wsh->error, NWD_DEVERR_ROW_RANGE);
     return;
   }
@@ -306,6 +313,7 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
   }
   if (tid == 0) S[B] = total32;
   __syncthreads();
+  if (early_plan) nwd::pdl_wait();
   // Work split.  Pair mode (small problems): CTA i takes the whole pair i, no
   // partials.  Otherwise every CTA takes an equal range [x0, x1) of the
   // flattened (pair, row) space, T = n_kv * all rows.
@@ -713,28 +721,34 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
 #pragma unroll
         for (int j = 0; j < NV; j++) dst[j] = o4[j];
       }
-      __threadfence();
+      // The consumer barrier orders every thread's partial before thread 0's
+      // ticket, whose release (gpu scope, cumulative) publishes them; the
+      // ticket's acquire and the barrier after it order the last CTA's loads
+      // of the other pieces after their publication.
       if (!consumer_sync(bar_csync, cph, abort_flag, &wsh->error)) break;
       if (ct == 0) {
-        const uint32_t t = atomicAdd(&tickets[b * p.n_kv + hkv], 1u);
+        const uint32_t t = atom_add_acq_rel_gpu(&tickets[b * p.n_kv + hkv], 1u);
         misc->last = (t == (uint32_t)(h.l - h.f)) ? 1 : 0;
       }
       if (!consumer_sync(bar_csync, cph, abort_flag, &wsh->error)) break;
       emit = misc->last != 0;
       if (emit) {
-        __threadfence();
         if (g < G) {
-          // one online pass over the pieces, 8 pieces' loads in flight per
-          // thread (the merge is L2-latency bound, not bandwidth bound)
+          // one online pass over the pieces, MB pieces' loads in flight per
+          // thread (the merge is L2-latency bound, not bandwidth bound, so
+          // every batch is one round trip): a single sequence over 8 kv heads
+          // has at most 20 pieces per pair, two batches; MB is the most that
+          // stays within registers
+          constexpr int MB = NV == 1 ? 12 : 10;
           M = -INFINITY;
           Ls = 0.f;
 #pragma unroll
           for (int j = 0; j < NV; j++) o4[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int32_t c0 = h.f; c0 <= h.l; c0 += 8) {
-            float2 ml[8];
-            float4 x[8][NV];
+          for (int32_t c0 = h.f; c0 <= h.l; c0 += MB) {
+            float2 ml[MB];
+            float4 x[MB][NV];
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
+            for (int j = 0; j < MB; j++) {
               const int32_t c = c0 + j;
               if (c <= h.l) {
                 // CTA f holds the pair's head in its tail slot; later CTAs in their head slot
@@ -750,7 +764,7 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
               }
             }
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
+            for (int j = 0; j < MB; j++) {
               if (ml[j].x == -INFINITY) continue;  // empty piece
               const float Mn = fmaxf(M, ml[j].x);
               const float a = ex2(M - Mn);  // 0 while M is -inf

@@ -46,6 +46,12 @@ static __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t pari
       : "memory");
   return ok != 0;
 }
+// Atomic add with acquire and release semantics at gpu scope; returns the old value.
+static __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 // Non-blocking test of a phase (never suspends the thread).
 static __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
