@@ -92,6 +92,7 @@ struct Params {
   uint32_t min_chunk;  // least rows (x kv heads) per CTA range
   uint32_t pair_max;   // one CTA per (sequence, kv head) when every pair is this short
   uint32_t split_k;    // > 0: CTA i takes piece i % k of pair i / k (k equal pieces per pair)
+  uint32_t prefetch;   // single sequence: K/V tiles per CTA prefetched into L2 before the wait
 };
 
 // ---- shared memory layout (offsets from a 1024-aligned base) ----
@@ -313,7 +314,6 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
   }
   if (tid == 0) S[B] = total32;
   __syncthreads();
-  if (early_plan) nwd::pdl_wait();
   // Work split.  Pair mode (small problems): CTA i takes the whole pair i, no
   // partials.  Otherwise every CTA takes an equal range [x0, x1) of the
   // flattened (pair, row) space, T = n_kv * all rows.
@@ -328,6 +328,36 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
   if (W < p.min_chunk) W = p.min_chunk;
   const uint64_t x0 = min(T, (uint64_t)blockIdx.x * W);
   const uint64_t x1 = min(T, x0 + W);
+
+  if (early_plan) {
+    // A single sequence: start this CTA's first K/V tiles on their way into L2
+    // while the previous kernel drains (the rows are read again by TMA after
+    // the wait; a row the previous kernel is still writing is updated in L2).
+    // A quarter of the range's tiles, at most p.prefetch: measured on
+    // back-to-back single-sequence steps, prefetching more (or at all for
+    // ranges of a few tiles) floods DRAM while the previous kernel's
+    // latency-bound merge still runs, and costs more than it hides.
+    if (warp == NCW && lane == 0 && !p.row_offset && total32 > 0 && p.prefetch > 0) {
+      const uint32_t L = total32;
+      uint64_t x = x0, xe = x1;
+      if (split_k) {
+        const uint32_t j = blockIdx.x % split_k, hkv = blockIdx.x / split_k;
+        x = (uint64_t)hkv * L + (uint64_t)j * L / split_k;
+        xe = hkv < p.n_kv ? (uint64_t)hkv * L + (uint64_t)(j + 1) * L / split_k : x;
+      }
+      uint32_t budget = min(p.prefetch, (uint32_t)(udiv64(xe - x, TOK) / 4u));
+      while (x < xe && budget > 0) {
+        const uint32_t hkv = (uint32_t)udiv64(x, L), t = (uint32_t)(x - (uint64_t)hkv * L);
+        const uint32_t n = (uint32_t)min((uint64_t)(L - t), xe - x);
+        for (uint32_t r = 0; r < n && budget > 0; r += TOK, budget--) {
+          tma_prefetch_4d(&tmk, 0, 0, (int)hkv, (int)(t + r));
+          tma_prefetch_4d(&tmv, 0, 0, (int)hkv, (int)(t + r));
+        }
+        x += n;
+      }
+    }
+    nwd::pdl_wait();
+  }
 
   // Empty sequences produce no rows, so no range covers them: CTA b % grid
   // writes their result (zeros, as the WGSL's untouched accumulator; or an
@@ -820,6 +850,7 @@ struct Tuning {
   uint32_t two_group_rows = 8192;  // single sequence: two groups from this many rows
   uint32_t short_rows = 2048;  // single sequence of at most this many rows: decode_short.cu
   uint32_t short_cta_rows = 128;  // past 256 rows: rows per CTA of a kv head's cluster
+  uint32_t prefetch = 8;  // single sequence: K/V tiles per CTA prefetched into L2 under PDL
 };
 
 uint32_t env_u32(const char* name, uint32_t dflt) {
@@ -842,6 +873,9 @@ const Tuning& tuning() {
     if (sr && *sr) x.short_rows = (uint32_t)strtoul(sr, nullptr, 10);
     if (x.short_rows > nwd::decode_short_max_rows()) x.short_rows = nwd::decode_short_max_rows();
     x.short_cta_rows = env_u32("NWD_DECODE_SHORT_CTA_ROWS", x.short_cta_rows);
+    // 0 turns the prefetch off
+    const char* pf = getenv("NWD_DECODE_PREFETCH");
+    if (pf && *pf) x.prefetch = (uint32_t)strtoul(pf, nullptr, 10);
     return x;
   }();
   return t;
@@ -967,6 +1001,7 @@ int launch(const Call& c) {
   p.append = c.append ? 1u : 0u;
   p.partial = c.partial ? 1u : 0u;
   p.min_chunk = tu.min_chunk;
+  p.prefetch = tu.prefetch;
   p.pair_max = tu.pair_max;
 
   // grid: one CTA per SM; for a single sequence (rows known here) one CTA per

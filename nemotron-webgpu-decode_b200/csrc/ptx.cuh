@@ -89,6 +89,15 @@ static __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, 
   const bool ok = mbar_wait(bar, parity, abort, dev_err);
   return __all_sync(0xffffffffu, ok);
 }
+// L2 prefetch of one tile (no shared memory, no barrier).  L2 is the point of
+// coherence, so it is safe even while another kernel may still write the rows.
+static __device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int c0, int c1, int c2,
+                                                int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
 static __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int c0, int c1, int c2, int c3, uint64_t policy) {
   asm volatile(
