@@ -118,8 +118,17 @@ __global__ void __launch_bounds__(STHREADS, 1)
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t g = lane >> 2, t = lane & 3;
 
-  // the previous kernel in the stream (e.g. the q/k/v projections) must be done
+  // the previous kernel in the stream (e.g. the q/k/v projections) must be
+  // done before any row is read; until then, start this CTA's K and V rows
+  // on their way into L2 (L2 is the point of coherence, so a row the previous
+  // kernel still writes is updated there before it is read after the wait)
   nwd::pdl_trigger();
+  for (uint32_t i = tid; i < 4 * n; i += STHREADS) {
+    // four 128-byte lines per row: K lo/hi, V lo/hi
+    const size_t at = ((size_t)(r_lo + (i >> 2)) * n_kv + hkv) * SHD + (i & 1) * 64;
+    const __half* src = (i & 2) ? vc + at : kc + at;
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(src) : "memory");
+  }
   nwd::pdl_wait();
 
   // ---- the head's K and V rows into shared memory ----
