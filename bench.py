@@ -355,6 +355,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--prefetch", action="store_true",
+                    help="config 6: prefetch the next projections' weights into L2 on a side stream")
     ap.add_argument("--batch", type=int, default=None,
                     help="config 3: only the first N sequences (small profiling captures)")
     ap.add_argument("--kv-len", type=int, default=None,
@@ -852,19 +854,24 @@ def run_config6(args, ops, torch, dist, dev, rank, world):
     step_bytes6 = weight_bytes + kv_bytes + act_bytes
 
     stream = torch.cuda.Stream(device=dev)
+    # optional weight prefetch: during each attention launch a side stream starts the
+    # layer's o_proj weights and the next layer's q/k/v weights into L2.  Off by
+    # default: measured slower (71.2 against 66.4 us per token), its HBM traffic
+    # lands on the latency-bound attention launch
+    side = torch.cuda.Stream(device=dev) if args.prefetch else None
     graphs = []
     with torch.cuda.stream(stream):
         for layers in sets:  # eager once (sets the kernels' attributes), then capture
-            for i, L in enumerate(layers):
+            for L in layers:
                 L.attn.seq = L6
-                L.step(h_norm[i], h)
+            eng.step_layers(layers, h_norm, h, side=side)
         torch.cuda.synchronize()
         for layers in sets:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
-                for i, L in enumerate(layers):
+                for L in layers:
                     L.attn.seq = L6
-                    L.step(h_norm[i], h)
+                eng.step_layers(layers, h_norm, h, side=side)
             graphs.append(g)
     torch.cuda.synchronize()
 
@@ -966,7 +973,11 @@ def run_config6(args, ops, torch, dist, dev, rank, world):
                        "weights_mb_per_step": weight_bytes / 1e6,
                        "bytes_per_step": step_bytes6,
                        "l2": "three rotating weight copies (296 MB) > L2",
-                       "launch": "CUDA graph per weight copy (12 launches)"},
+                       "weight_prefetch": ("off" if side is None else
+                                           "each layer's o_proj and the next layer's q/k/v "
+                                           "weights into L2 on a side stream during attention"),
+                       "launch": "CUDA graph per weight copy (12 launches, + 4 "
+                                 "prefetch launches on the side stream)"},
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
                          "frac": gbs / peak, "kernel": "q4_gemv_kernel (q/k/v + append)",
                          "launch_ms": qkv_max, "bytes_per_launch": qkv_bytes,
@@ -976,7 +987,7 @@ def run_config6(args, ops, torch, dist, dev, rank, world):
                      "h2d_bytes_per_step": N_ATTN_LAYERS * HIDDEN6 * 4,
                      "d2h_bytes_per_step": HIDDEN6 * 4} if e2e is not None else None),
             "cpu_baseline": cpu,
-            "gpu_launches": 12 * args.steps,
+            "gpu_launches": (12 if side is None else 16) * args.steps,
             "device_error": err,
             "clocks": sampler.summary(t0, t1) if sampler else None,
         }

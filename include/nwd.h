@@ -245,6 +245,13 @@ int nwd_q4_qkv_append(const float* h, const uint32_t* bq, const float* sq, const
                       uint16_t* v_cache, uint32_t seq, uint32_t cap, uint32_t K,
                       uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim, void* stream);
 
+/* L2 prefetch of up to 16 device buffers (ptrs[i], bytes[i]; host arrays),
+ * e.g. the next projection's q4 weights, issued on a side stream while a
+ * latency-bound kernel leaves HBM idle.  A hint only: it moves no data into
+ * any SM, orders nothing and never changes a result.  No counterpart in the
+ * reference (runtime.js:385-394 runs the layer's dispatches back to back). */
+int nwd_prefetch_l2(const void* const* ptrs, const uint64_t* bytes, uint32_t n, void* stream);
+
 /* ------------------------------------------------------------------ */
 /* Prompt chunks (causal prefill)                                      */
 /* ------------------------------------------------------------------ */

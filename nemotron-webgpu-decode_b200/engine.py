@@ -115,14 +115,28 @@ class AttentionLayer:
     def seq(self) -> int:
         return self.attn.seq
 
-    def step(self, h_norm: torch.Tensor, h: torch.Tensor, stream=None) -> torch.Tensor:
+    def qkv_weights(self) -> list:
+        """The q / k / v weight buffers (what the layer's first launch reads)."""
+        return [t for w in (self.wq, self.wk, self.wv) for t in (w.b, w.scales, w.zp)]
+
+    def step(self, h_norm: torch.Tensor, h: torch.Tensor, stream=None,
+             prefetch=None) -> torch.Tensor:
         """h += o_proj(attention(q, K, V)) for this token; h_norm [hidden] f32 is the
-        layer's normalised input, h [hidden] f32 the residual stream (updated in place)."""
+        layer's normalised input, h [hidden] f32 the residual stream (updated in place).
+
+        prefetch = (side_stream, buffers): once the q/k/v launch is done, side_stream
+        starts this layer's o_proj weights and `buffers` (e.g. the next layer's
+        :meth:`qkv_weights`) into L2 while attention runs; the caller joins
+        side_stream before it next needs it.  Results do not change."""
         a = self.attn
         if a.seq >= a.max_seq:
             raise NwdError(NWD_ERR_RANGE, f"seq {a.seq} exceeds maxSeq {a.max_seq}")
         ops.q4_qkv_append(h_norm, self.wq, self.wk, self.wv, self.q, a.k_cache, a.v_cache,
                           a.seq, stream=stream)
+        if prefetch is not None:
+            side, extra = prefetch
+            side.wait_stream(stream if stream is not None else torch.cuda.current_stream())
+            ops.prefetch_l2([self.wo.b, self.wo.scales, self.wo.zp] + list(extra), stream=side)
         ops.attention(self.q, a.k_cache, a.v_cache, self.o,
                       ops.AttnParams(a.heads, a.kv_heads, a.head_dim, a.seq + 1),
                       scale=a.scale, workspace=a.workspace, stream=stream)
@@ -132,6 +146,21 @@ class AttentionLayer:
 
     def reset(self) -> None:
         self.attn.reset()
+
+
+def step_layers(layers, h_norm: torch.Tensor, h: torch.Tensor, side=None, stream=None):
+    """One token through consecutive attention layers (h_norm [n_layers, hidden]).  With a
+    side stream, each layer's o_proj weights and the next layer's q/k/v weights are
+    prefetched into L2 during its attention launch; the side stream is joined at the end."""
+    cur = stream if stream is not None else torch.cuda.current_stream()
+    for i, layer in enumerate(layers):
+        pf = None
+        if side is not None:
+            pf = (side, layers[i + 1].qkv_weights() if i + 1 < len(layers) else [])
+        layer.step(h_norm[i], h, stream=stream, prefetch=pf)
+    if side is not None:
+        cur.wait_stream(side)
+    return h
 
 
 class BatchedDecodeAttention:

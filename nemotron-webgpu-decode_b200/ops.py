@@ -371,6 +371,20 @@ def q4_qkv_append(h: torch.Tensor, wq: Q4Weights, wk: Q4Weights, wv: Q4Weights,
     return q_out
 
 
+def prefetch_l2(buffers, stream=None) -> None:
+    """Start up to 16 CUDA tensors (e.g. the next projection's q4 weights) on their way
+    into L2 on `stream`.  A hint: it never changes a result."""
+    buffers = list(buffers)
+    for i, t in enumerate(buffers):
+        if not isinstance(t, torch.Tensor) or not t.is_cuda or not t.is_contiguous():
+            raise ValueError(f"buffer {i} must be a contiguous CUDA tensor")
+    n = len(buffers)
+    ptrs = (ctypes.c_void_p * max(n, 1))(*[t.data_ptr() for t in buffers])
+    sizes = (ctypes.c_uint64 * max(n, 1))(*[t.numel() * t.element_size() for t in buffers])
+    call("nwd_prefetch_l2", ctypes.cast(ptrs, ctypes.c_void_p), ctypes.cast(sizes, ctypes.c_void_p),
+         n, _stream(stream))
+
+
 def fill_normal(t: torch.Tensor, seed: int, offset: int = 0, stream=None) -> torch.Tensor:
     """Fill an fp16 tensor with the deterministic N(0,1) stream (bit-identical to the CPU
     generator used by the tests)."""

@@ -80,3 +80,21 @@ def test_ops_reject_cpu_tensors(ops):
     cache = torch.zeros(256, 8, 128, dtype=torch.float16)
     with pytest.raises(ValueError, match="CUDA tensor"):
         ops.kv_append(src, cache, ops.KvParams(0, 8, 128))
+
+
+def test_prefetch_argument_errors_before_launch(nwd):
+    """nwd_prefetch_l2 refuses more than 16 ranges and null pointers before any CUDA
+    call; zero ranges (or only empty ones) is a no-op."""
+    from importlib import import_module
+    _lib = import_module(nwd.__name__ + "._lib")
+    lib = _lib.load()
+    ptrs = (ctypes.c_void_p * 17)(*([16] * 17))
+    sizes = (ctypes.c_uint64 * 17)(*([64] * 17))
+    assert lib.nwd_prefetch_l2(ptrs, sizes, 17, None) == _lib.NWD_ERR_INVALID
+    assert b"at most 16" in lib.nwd_last_error()
+    assert lib.nwd_prefetch_l2(None, None, 2, None) == _lib.NWD_ERR_INVALID
+    null = (ctypes.c_void_p * 1)(None)
+    assert lib.nwd_prefetch_l2(null, sizes, 1, None) == _lib.NWD_ERR_INVALID
+    assert lib.nwd_prefetch_l2(None, None, 0, None) == _lib.NWD_OK
+    empty = (ctypes.c_uint64 * 1)(0)
+    assert lib.nwd_prefetch_l2(null, empty, 1, None) == _lib.NWD_OK

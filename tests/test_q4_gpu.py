@@ -140,3 +140,67 @@ def test_attention_layer_steps(engine_mod, ops, oracle):
         h = got.astype(np.float32)  # follow the kernel's residual stream
     assert layer.seq == 6
     assert layer.attn.workspace.check() == 0
+
+
+def test_layers_with_weight_prefetch(engine_mod, ops, oracle):
+    """engine.step_layers with the side-stream L2 weight prefetch gives bit-identical
+    results to the same layers without it (the prefetch is only a hint), eager and
+    captured in a CUDA graph."""
+    K, nh, nkv, hd, cap, n_layers = 3136, 40, 8, 128, 256, 3
+
+    def make():
+        layers = []
+        for i in range(n_layers):
+            ws = [_weights(ops, oracle, n, nb, seed=300 + 4 * i + j)[0] for j, (n, nb) in
+                  enumerate([(nh * hd, K // 32), (nkv * hd, K // 32), (nkv * hd, K // 32),
+                             (K, nh * hd // 32)])]
+            layer = engine_mod.AttentionLayer(*ws, nh, nkv, hd, cap)
+            ops.fill_normal(layer.attn.k_cache, 70 + i)
+            ops.fill_normal(layer.attn.v_cache, 80 + i)
+            layer.attn.seq = 150
+            layers.append(layer)
+        return layers
+
+    hn = torch.from_numpy(np.stack([_act(oracle, K, seed=400 + i) for i in range(n_layers)])).cuda()
+    h0 = torch.from_numpy(_act(oracle, K, seed=450)).cuda()
+    plain, pref = make(), make()
+    h_plain, h_pref = h0.clone(), h0.clone()
+    engine_mod.step_layers(plain, hn, h_plain)
+    side = torch.cuda.Stream()
+    engine_mod.step_layers(pref, hn, h_pref, side=side)
+    torch.cuda.synchronize()
+    assert torch.equal(h_plain, h_pref)
+    for a, b in zip(plain, pref):
+        assert torch.equal(a.attn.k_cache, b.attn.k_cache)
+        assert torch.equal(a.attn.v_cache, b.attn.v_cache)
+        assert a.seq == b.seq == 151
+    # captured: fork and join of the side stream inside the graph
+    stream = torch.cuda.Stream()
+    for layer in pref:
+        layer.attn.seq = 150
+    for layer in plain:
+        layer.attn.seq = 150
+    h_plain.copy_(h0)
+    engine_mod.step_layers(plain, hn, h_plain)
+    with torch.cuda.stream(stream):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            engine_mod.step_layers(pref, hn, h_pref, side=side)
+        h_pref.copy_(h0)
+        g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(h_plain, h_pref)
+    assert all(layer.attn.workspace.check() == 0 for layer in plain + pref)
+
+
+def test_prefetch_l2_arguments(ops):
+    """Ragged sizes and unaligned starts are accepted (the aligned interior is
+    prefetched); more than 16 buffers or non-CUDA tensors are refused."""
+    x = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda")
+    ops.prefetch_l2([x[1:], x[:7], x[16:4096 + 16]])
+    ops.prefetch_l2([])
+    torch.cuda.synchronize()
+    with pytest.raises(ops.NwdError):
+        ops.prefetch_l2([x] * 17)
+    with pytest.raises(ValueError):
+        ops.prefetch_l2([torch.zeros(4)])
