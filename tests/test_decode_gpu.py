@@ -48,6 +48,16 @@ def test_group_sizes(ops, oracle, nh, nkv):
     assert_attn_close(got, ref, f"Hq={nh} Hkv={nkv}")
 
 
+@pytest.mark.parametrize("nh,nkv,L", [(8, 8, 3000), (64, 8, 3000), (16, 2, 9000), (5, 1, 12000),
+                                      (3, 1, 2049), (40, 8, 2049)])
+def test_group_sizes_split(ops, oracle, nh, nkv, L):
+    """Group sizes on the split-KV kernel (past the short kernel's 2 048 rows): with one or
+    two kv heads a pair is cut into up to one piece per SM, so the last CTA merges up
+    to ~148 partials (many batches of loads) and every CTA's range prefetch differs."""
+    got, ref = _single(ops, oracle, nh, nkv, L, L + 7, seed=91 + L)
+    assert_attn_close(got, ref, f"Hq={nh} Hkv={nkv} L={L}")
+
+
 @pytest.mark.parametrize("nh,nkv,L", [(8, 8, 151), (16, 8, 33), (24, 8, 151), (56, 8, 200),
                                       (64, 8, 256), (16, 2, 97), (5, 1, 151), (3, 1, 1)])
 def test_group_sizes_short(ops, oracle, nh, nkv, L):
