@@ -1081,6 +1081,7 @@ def run_config5(args, ops, torch, dist, dev, rank, world):
     kern_ms = statistics.mean(x.elapsed_time(y) for x, y in evs)
     local_rows = sum(hi - lo for lo, hi in (sd.global_rows(b) for b in range(B)))
     kern_bytes = 4096.0 * local_rows + B * HQ * HD * 2 + B * HQ * (HD + 2) * 4
+    traffic5 = profiled_traffic("decode_kernel_config5_traffic")
     # e2e: q from pinned host memory, O back to host, every step
     q_h = q.cpu().pin_memory()
     o_h = torch.empty(B, HQ, HD, dtype=torch.float16, pin_memory=True)
@@ -1121,7 +1122,11 @@ def run_config5(args, ops, torch, dist, dev, rank, world):
                          "peak": peak, "unit": "GB/s",
                          "frac": kern_bytes / (kern_ms * 1e-3) / 1e9 / peak,
                          "kernel": "decode_kernel (partial mode), per rank",
-                         "launch_ms": kern_ms, "peak_source": kind},
+                         "launch_ms": kern_ms, "peak_source": kind,
+                         # committed ncu figure for the whole 1-GPU launch (4 x 2^20 rows),
+                         # scaled to this rank's rows (traffic is proportional to rows)
+                         "traffic": (None if traffic5 is None else
+                                     traffic5 * local_rows / (4.0 * (1 << 20)))},
             "e2e": {"value": B * args.steps / (e2e_max * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": B * HQ * HD * 2, "d2h_bytes_per_step": B * HQ * HD * 2},
             "gpu_launches": 2 * args.steps,

@@ -62,7 +62,8 @@ def test_clock_summary_without_nvidia_smi(bench):
     assert c["samples"] == 0 and c["sm_mhz"] is None and "unavailable" in c["note"]
 
 
-@pytest.mark.parametrize("name", ["decode_kernel_config3_traffic", "q4_gemv_kernel_config6_traffic"])
+@pytest.mark.parametrize("name", ["decode_kernel_config3_traffic", "decode_kernel_config5_traffic",
+                                  "q4_gemv_kernel_config6_traffic"])
 def test_profiled_traffic_files(bench, name):
     v = bench.profiled_traffic(name)
     assert v is not None and v > 0
