@@ -43,6 +43,8 @@ def _case(ops, oracle, batch, n_q, start_pos, nh, nkv, seed, extra=0):
     (1, 256, 300, 8, 2),   # chunk after 300 cached rows: unaligned key blocks
     (2, 129, 0, 40, 8),    # engine shape, group 5
     (1, 1, 777, 32, 8),    # one token: a decode step through the prefill kernel
+    (3, 300, 45, 64, 8),   # group 8, three sequences of three tiles each, unaligned start
+    (4, 260, 1000, 16, 2), # long cached prefix: many key blocks before the diagonal
 ])
 def test_prefill_vs_oracle(ops, oracle, batch, n_q, start_pos, nh, nkv):
     got, ref = _case(ops, oracle, batch, n_q, start_pos, nh, nkv, seed=batch * 100 + n_q)
