@@ -9,7 +9,6 @@ import pytest
 import torch
 
 from devutil import bits, to_dev, vals
-from tolerance import assert_attn_close
 
 pytestmark = pytest.mark.gpu
 
