@@ -71,3 +71,29 @@ def test_profiled_traffic_files(bench, name):
 
 def test_profiled_traffic_missing_file(bench):
     assert bench.profiled_traffic("no_such_profile") is None
+
+
+def test_reference_arm_line(tmp_path):
+    """bench.py --impl reference (the CPU reference arm the driver runs beside the GPU arm)
+    prints one JSON line with the contract's keys, on CPU alone; under torchrun only rank 0
+    prints and the other ranks exit 0."""
+    import json
+    import subprocess
+    import sys
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    cmd = [sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference", "--steps", "1",
+           "--warmup", "3"]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=600, cwd=REPO)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+              "higher_is_better", "config", "impl", "cpu_baseline", "e2e"):
+        assert k in d, k
+    assert d["impl"] == "reference" and d["value"] > 0
+    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["value"] == d["value"]
+    env["RANK"] = "1"
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=600, cwd=REPO)
+    assert r.returncode == 0 and not [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
