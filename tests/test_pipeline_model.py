@@ -138,6 +138,56 @@ def test_planner_bench_shapes():
     assert sizes[-1] - sizes[1] <= 0
 
 
+def prefetch_rows(L, nkv, grid, cta, split_k=0, min_chunk=256, cap=8):
+    """The (kv head, first row) of the K/V tiles CTA `cta` prefetches into L2 before its
+    dependency wait, for a single sequence of L rows: csrc/decode.cu's restatement."""
+    T = nkv * L
+    W = max((T + grid - 1) // grid, min_chunk)
+    x0, x1 = min(T, cta * W), min(T, cta * W + W)
+    x, xe = x0, x1
+    if split_k:
+        j, h = cta % split_k, cta // split_k
+        x = h * L + j * L // split_k
+        xe = h * L + (j + 1) * L // split_k if h < nkv else x
+    budget = min(cap, ((xe - x) // TOK) // 4) if xe > x else 0
+    out = []
+    while x < xe and budget > 0:
+        h, t = divmod(x, L)
+        n = min(L - t, xe - x)
+        r = 0
+        while r < n and budget > 0:
+            out.append((h, t + r))
+            r += TOK
+            budget -= 1
+        x += n
+    return out
+
+
+@pytest.mark.parametrize("L,nkv", [(2049, 8), (4096, 8), (16384, 8), (32768, 8), (262144, 8),
+                                   (12000, 1), (9000, 2), (5000, 3)])
+def test_prefetch_stays_inside_the_ctas_pieces(L, nkv):
+    """Every tile a CTA prefetches starts on a row its own pieces stream (so the
+    prefetch only moves bytes that CTA reads right after the wait), there are a
+    quarter of its range's whole tiles (at most 8), and they are its first ones."""
+    for split in (True, False):
+        grid, k = host_split(L, nkv)
+        if not split:
+            grid, k = 148, 0
+        pieces, _ = plan([L], nkv, grid, split_k=k)
+        for cta in range(grid):
+            mine = [(h, t0, t1) for (i, b, h, t0, t1, *_rest) in pieces if i == cta]
+            tiles = prefetch_rows(L, nkv, grid, cta, split_k=k)
+            rows = sum(t1 - t0 for _, t0, t1 in mine)
+            assert len(tiles) == min(8, (rows // TOK) // 4)
+            for h, r in tiles:
+                assert any(h == ph and t0 <= r < t1 for ph, t0, t1 in mine)
+            # the first tiles of the range, in stream order
+            expect = []
+            for h, t0, t1 in mine:
+                expect += [(h, r) for r in range(t0, t1, TOK)]
+            assert tiles == expect[:len(tiles)]
+
+
 def test_planner_random_shapes():
     rng = np.random.default_rng(0)
     for _ in range(200):
