@@ -158,3 +158,55 @@ def test_f64_and_f32_restatements_agree_long(oracle):
     a = oracle.attention_batched(q, k, v, [0], [L], nh, nkv, hd)
     b = oracle.attention_batched(q, k, v, [0], [L], nh, nkv, hd, f64=True)
     assert np.abs(a - b).max() < 2e-5
+
+
+def _q4_numpy_f64(a, B, scales, zp):
+    """kernels/matmul_nbits_sg.wgsl:25-72 restated in numpy float64, independently of the
+    C oracle: element j of word w of block blk is bits [4j, 4j+4) of B[n, blk, w] (the
+    shader's lo/hi byte-nibble interleave, :37-40) and multiplies A[32*blk + 8*w + j];
+    the zero point of (n, blk) is nibble n*n_blocks + blk of zp (:25-28)."""
+    n, nb = scales.shape
+    shifts = (4 * np.arange(8, dtype=np.uint32))[None, None, None, :]
+    q = ((B.astype(np.uint32)[..., None] >> shifts) & 15).reshape(n, nb, 32).astype(np.float64)
+    idx = np.arange(n * nb).reshape(n, nb)
+    z = ((zp[idx // 8] >> ((idx % 8) * 4).astype(np.uint32)) & 15).astype(np.float64)
+    a64 = np.asarray(a, np.float64).reshape(nb, 32)
+    return (((q - z[..., None]) * a64[None]).sum(-1) * scales.astype(np.float64)).sum(-1)
+
+
+@pytest.mark.parametrize("n,n_blocks", [(7, 1), (40, 98), (33, 160)])
+def test_q4_gemv_oracle_vs_numpy(oracle, n, n_blocks):
+    """The oracle's q4 GEMV (the parity reference for the projections around the path)
+    against an independent float64 numpy restatement of the shader, and its epilogues."""
+    B, scales, zp = oracle.q4_weights(n, n_blocks, seed=n + n_blocks)
+    a = oracle.f16_bits_to_f32(oracle.normal_f16(32 * n_blocks, 5))
+    ref = _q4_numpy_f64(a, B, scales, zp)
+    np.testing.assert_allclose(oracle.q4_gemv_f64(a, B, scales, zp), ref, rtol=1e-12, atol=1e-9)
+    tol = 1e-5 * max(float(np.abs(ref).max()), 1.0)
+    got = oracle.q4_gemv(a, B, scales, zp)
+    assert float(np.abs(got - ref).max()) <= tol
+    relu2 = np.maximum(ref, 0.0) ** 2
+    got1 = oracle.q4_gemv(a, B, scales, zp, epilogue=1)
+    assert float(np.abs(got1 - relu2).max()) <= 1e-5 * max(float(np.abs(relu2).max()), 1.0)
+    y0 = np.linspace(-1, 1, n).astype(np.float32)
+    got2 = oracle.q4_gemv(a, B, scales, zp, epilogue=2, y=y0)
+    assert float(np.abs(got2 - (y0 + ref)).max()) <= tol
+
+
+def test_prefill_oracle_is_one_decode_step_per_token(oracle):
+    """The prefill oracle is the reference's prompt loop (engine/runtime.js:640-643):
+    token i of a chunk starting at row start_pos is a decode step over rows
+    0..start_pos+i, bit-identical to the decode oracle on the same rows."""
+    nh, nkv, hd, n_q, start, batch = 4, 2, 128, 5, 3, 2
+    rows = start + n_q
+    kp = oracle.normal_f16(batch * rows * nkv * hd, 71).reshape(batch * rows, nkv, hd)
+    vp = oracle.normal_f16(batch * rows * nkv * hd, 72).reshape(batch * rows, nkv, hd)
+    q = oracle.normal_f16(batch * n_q * nh * hd, 73).reshape(batch, n_q, nh, hd)
+    offs = np.arange(batch, dtype=np.int64) * rows
+    pre = oracle.attention_prefill(q, kp, vp, offs, n_q, start, nh, nkv, hd)
+    for b in range(batch):
+        for i in range(n_q):
+            k = kp[offs[b]: offs[b] + rows]
+            v = vp[offs[b]: offs[b] + rows]
+            step = oracle.attention(q[b, i], k, v, nh, nkv, hd, start + i + 1)
+            assert np.array_equal(pre[b, i], step), (b, i)
