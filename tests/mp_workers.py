@@ -73,3 +73,47 @@ def max_over_ranks_worker(rank, world, port, repo, outdir):
                    "seeds": bench.seeds_for(rank)}, f)
     dist.barrier()
     dist.destroy_process_group()
+
+
+def missing_rank_worker(rank, world, port, repo, outdir):
+    """Failure detection on the host: rank 1 leaves between steps without posting its
+    shard partials (injected on the host, no GPU involved); rank 0's sharded step must
+    end with an error once the process group's deadline passes, not hang."""
+    sys.path[:0] = [repo]
+    import datetime
+    import time
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    deadline = 3.0
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=deadline))
+    mgpu = importlib.import_module("nemotron-webgpu-decode_b200.mgpu")
+    B, nh, nkv, hd = 2, 4, 2, 128
+
+    def partial_fn(q):
+        return torch.zeros(B, nh, hd), torch.full((B, nh, 2), 1.0)
+
+    def merge_fn(go, gml, out):
+        return out
+
+    sd = mgpu.ShardedDecode([300, 77], nh, nkv, hd, partial_fn=partial_fn, merge_fn=merge_fn)
+    out = torch.empty(B, nh, hd, dtype=torch.float32)
+    sd.step(None, out=out)  # one good step with every rank present
+    if rank == world - 1:
+        # the failing rank: stays alive but never posts its next partials
+        with open(os.path.join(outdir, f"rank{rank}.json"), "w") as f:
+            json.dump({"left": True}, f)
+        time.sleep(3 * deadline)
+        os._exit(0)
+    t0 = time.monotonic()
+    try:
+        sd.step(None, out=out)
+        status = "completed"
+    except Exception as e:  # the collective's deadline
+        status = f"{type(e).__name__}: {str(e)[:160]}"
+    elapsed = time.monotonic() - t0
+    with open(os.path.join(outdir, f"rank{rank}.json"), "w") as f:
+        json.dump({"status": status, "elapsed": elapsed, "deadline": deadline}, f)
+    os._exit(0)  # the group is broken: no collective teardown

@@ -51,3 +51,14 @@ def test_bench_rank_helpers(tmp_path):
     assert res[0]["seeds"] != res[1]["seeds"]
     L = np.random.default_rng(3).integers(512, 8193, 256)
     assert res[0]["strong"] + res[1]["strong"] == [int(x) for x in L]
+
+
+def test_missing_rank_ends_the_step_with_an_error(tmp_path):
+    """A rank that stops posting its shard partials (host-side injection) makes the
+    other ranks' sharded step fail once the process group's deadline passes, instead of
+    waiting for ever; no GPU is involved."""
+    res = _run(mp_workers.missing_rank_worker, 2, tmp_path)
+    assert res[1] == {"left": True}
+    r0 = res[0]
+    assert r0["status"] != "completed", r0
+    assert r0["elapsed"] < 10 * r0["deadline"], r0
