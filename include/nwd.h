@@ -110,6 +110,14 @@ int nwd_workspace_check(void* workspace, size_t ws_bytes, uint32_t* device_error
 #define NWD_DEVERR_PIPE_TIMEOUT 1u  /* an mbarrier wait hit its iteration limit */
 #define NWD_DEVERR_ROW_RANGE 2u     /* a row index fell outside the pool */
 
+/* Failure-detection self-test: launches one CTA whose bounded mbarrier wait
+ * (the one every kernel here uses) is made to run out; after about 2 s the
+ * kernel returns and the workspace's error word holds
+ * NWD_DEVERR_PIPE_TIMEOUT (read it with nwd_workspace_check).  The stream and
+ * the context stay usable.  No counterpart in the reference (its waits are
+ * WebGPU barriers; failures surface through error scopes, runtime.js:474-487). */
+int nwd_selftest_wait_timeout(void* workspace, size_t ws_bytes, void* stream);
+
 /* Softmax `scale` below: finite and >= 0; 0 selects the reference's
  * inverseSqrt(head_dim). */
 

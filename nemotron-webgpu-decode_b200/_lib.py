@@ -71,6 +71,7 @@ SIGNATURES = {
     "nwd_attn_merge_packed": (ctypes.c_int, [_P, _P, _u32, _u32, _u32, _u32, _P]),
     "nwd_q4_gemv": (ctypes.c_int, [_P, _P, _P, _P, _P, _u32, _u32, _u32, _u32, _P]),
     "nwd_prefetch_l2": (ctypes.c_int, [_P, _P, _u32, _P]),
+    "nwd_selftest_wait_timeout": (ctypes.c_int, [_P, _sz, _P]),
     "nwd_q4_gemv_f16a": (ctypes.c_int, [_P, _P, _P, _P, _P, _u32, _u32, _u32, _u32, _P]),
     "nwd_q4_qkv_append": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                          _u32, _u32, _u32, _u32, _u32, _u32, _P]),

@@ -371,6 +371,14 @@ def q4_qkv_append(h: torch.Tensor, wq: Q4Weights, wk: Q4Weights, wv: Q4Weights,
     return q_out
 
 
+def selftest_wait_timeout(workspace: "Workspace", stream=None) -> int:
+    """Make one of the library's bounded device waits run out (about 2 s) and return the
+    workspace's device error word afterwards (NWD_DEVERR_PIPE_TIMEOUT expected); the
+    stream stays usable."""
+    call("nwd_selftest_wait_timeout", workspace.ptr, workspace.nbytes, _stream(stream))
+    return workspace.check(stream)
+
+
 def prefetch_l2(buffers, stream=None) -> None:
     """Start up to 16 CUDA tensors (e.g. the next projection's q4 weights) on their way
     into L2 on `stream`.  A hint: it never changes a result."""
