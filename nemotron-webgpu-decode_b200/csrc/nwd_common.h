@@ -52,7 +52,9 @@ int launch_decode_short(const uint16_t* q, const uint16_t* k_new, const uint16_t
 // the kernel after it may start early in turn) and pdl_wait() in every CTA, on
 // every path, before it reads or writes memory that another kernel writes or
 // reads: pdl_wait() returns once the previous kernel has completed and its
-// writes are visible.  Before it, only constant inputs (weights) are read.
+// writes are visible.  Before it, only constant inputs (weights) are read;
+// other memory may only be prefetched into L2 (which brings nothing into the
+// SM and, L2 being the point of coherence, never yields a stale value).
 // Because every CTA waits, a kernel completes only after the one before it,
 // so ordering stays transitive along the stream.
 #ifdef __CUDACC__
