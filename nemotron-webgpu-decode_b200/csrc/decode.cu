@@ -921,6 +921,13 @@ int check_shape(uint32_t n_heads, uint32_t n_kv, uint32_t hd, const char* who) {
   return NWD_OK;
 }
 
+// A single sequence of at most tu.short_rows rows (not a shard partial) runs
+// on decode_short_kernel, which uses no workspace.
+bool takes_short_path(const Call& c, const Tuning& tu) {
+  return !c.seq_len && !c.partial && c.single_len >= 1 &&
+         (uint32_t)c.single_len <= tu.short_rows;
+}
+
 int launch(const Call& c) {
   using namespace nwd;
   int st = check_shape(c.n_heads, c.n_kv, c.hd, c.who);
@@ -956,8 +963,7 @@ int launch(const Call& c) {
     return fail(NWD_ERR_INVALID, "%s: scale must be finite and >= 0 (0 = 1/sqrt(head_dim))", c.who);
 
   // one short sequence: a cluster of CTAs per kv head (no workspace use)
-  if (!c.seq_len && !c.partial && c.single_len >= 1 &&
-      (uint32_t)c.single_len <= tu.short_rows) {
+  if (takes_short_path(c, tu)) {
     const float sc = c.scale != 0.f ? c.scale : 1.0f / sqrtf((float)c.hd);
     return launch_decode_short(c.q, c.k_new, c.v_new, const_cast<uint16_t*>(c.k_pool),
                                const_cast<uint16_t*>(c.v_pool), c.o, (uint32_t)c.single_len,
@@ -1067,20 +1073,36 @@ constexpr size_t NOALLOC_BYTES =
     (size_t)2 * NOALLOC_MAX_SMS * GMAX * HD * sizeof(float) /* o per slot and head */;
 __device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_BYTES];
 
+constexpr int NOALLOC_MAX_DEVICES = 64;
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[64] = {};
+void* g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
 
 // Device address of the scratch on the current device.  Host code only sees
 // a host-side stand-in for a __device__ array, so the address is looked up
-// once per device (with that device current) and cached.
-int noalloc_scratch(int device, void** out) {
+// with the device current.  It is looked up again on every call made outside
+// stream capture (a cheap query once the module is loaded, and it stays right
+// after a cudaDeviceReset reloads the module); a call made while `stream` is
+// being captured reuses the address of the device's last uncaptured call,
+// since the first lookup may load the module, which capture does not allow.
+int noalloc_scratch(int device, void* stream, void** out) {
   using namespace nwd;
+  if (device < 0 || device >= NOALLOC_MAX_DEVICES)
+    return fail(NWD_ERR_UNSUPPORTED, "built-in decode scratch: device %d >= %d", device,
+                NOALLOC_MAX_DEVICES);
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing((cudaStream_t)stream, &cap);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_ptr[device]) {
+  if (cap == cudaStreamCaptureStatusNone) {
     void* ptr = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(decode scratch)");
     g_noalloc_ptr[device] = ptr;
+  } else if (!g_noalloc_ptr[device]) {
+    return fail(NWD_ERR_CUDA,
+                "built-in decode scratch: the first call on device %d was made during stream "
+                "capture; make one call before capturing",
+                device);
   }
   *out = g_noalloc_ptr[device];
   return NWD_OK;
@@ -1139,18 +1161,35 @@ int nwd_attn_decode_noalloc(const uint16_t* q, const uint16_t* k_cache, const ui
                 "holds %zu",
                 who, lay.total, di.sm_count, NOALLOC_BYTES);
   void* scratch = nullptr;
-  st = noalloc_scratch(di.device, &scratch);
+  st = noalloc_scratch(di.device, stream, &scratch);
   if (st) return st;
-  // The scratch keeps the previous call's contents: the header and merge
-  // tickets must start at zero, so clear them (no allocation involved).
-  cudaError_t e = cudaMemsetAsync(scratch, 0, lay.ml_off, (cudaStream_t)stream);
-  if (e != cudaSuccess) return cuda_fail(e, "clearing the decode scratch");
   Call c{};
   c.q = q; c.k_pool = k_cache; c.v_pool = v_cache; c.pool_rows = cap;
   c.single_len = (int32_t)seq; c.o = o; c.batch = 1;
   c.n_heads = n_heads; c.n_kv = n_kv_heads; c.hd = head_dim; c.scale = scale;
   c.ws = scratch; c.ws_bytes = NOALLOC_BYTES; c.stream = stream; c.who = who;
+  if (!takes_short_path(c, tuning()) && seq > 0) {
+    // The scratch keeps the previous call's contents.  The merge tickets must
+    // start at zero; a completed call leaves them so, one that gave up on a
+    // wait may not, so clear them (a memset, no allocation).  The header's
+    // error word is left for nwd_noalloc_check to read.
+    cudaError_t e = cudaMemsetAsync(static_cast<uint8_t*>(scratch) + lay.tickets_off, 0,
+                                    lay.ml_off - lay.tickets_off, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "clearing the decode scratch's merge tickets");
+  }
   return launch(c);
+}
+
+int nwd_noalloc_check(uint32_t* device_error, void* stream) {
+  if (!device_error) return fail(NWD_ERR_INVALID, "nwd_noalloc_check: device_error is NULL");
+  DeviceInfo di;
+  int st = current_device_info(&di);
+  if (st) return st;
+  void* scratch = nullptr;
+  st = noalloc_scratch(di.device, stream, &scratch);
+  if (st) return st;
+  // the error word is the scratch header's first word, as in a caller workspace
+  return nwd_workspace_check(scratch, sizeof(WsHeader), device_error, stream);
 }
 
 int nwd_kv_append_attn_decode(const uint16_t* q, const uint16_t* k_new, const uint16_t* v_new,

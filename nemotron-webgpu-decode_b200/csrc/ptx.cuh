@@ -1,8 +1,11 @@
 // PTX building blocks shared by the library's kernels: shared-memory
 // addresses, the global timer, mbarriers with bounded waits, TMA and bulk
-// copies, L2 cache policies.  Every wait gives up after WAIT_LIMIT_NS (or
-// WAIT_LIMIT_ITERS polls), raises the caller's abort flag and records
-// NWD_DEVERR_PIPE_TIMEOUT, so no kernel here can spin forever.
+// copies, L2 cache policies.  Every wait gives up after WAIT_LIMIT_NS of the
+// global timer (2 s), raises the caller's abort flag and records
+// NWD_DEVERR_PIPE_TIMEOUT, so no kernel here can spin forever.  A count of
+// WAIT_LIMIT_ITERS polls is only a backstop should the timer not advance: a
+// poll takes well over 2 s / 2^30 (about 2 ns), so the timer ends every wait
+// first.
 #pragma once
 
 #include <cuda.h>
@@ -14,7 +17,7 @@ namespace nwd {
 namespace ptx {
 
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s
-constexpr uint32_t WAIT_LIMIT_ITERS = 1u << 26;
+constexpr uint32_t WAIT_LIMIT_ITERS = 1u << 30;  // backstop only
 
 // ---------------- PTX wrappers ----------------
 static __device__ __forceinline__ uint32_t smem_u32(const void* p) {
