@@ -146,12 +146,21 @@ int nwd_attn_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* 
  * device address; make that first call before any stream capture.  All calls
  * share the one scratch: calls that may overlap on the GPU (different
  * streams, or different host threads) race and must be serialised by the
- * caller.  Each call clears the scratch's header on `stream` before its
- * launch.  No counterpart in the reference. */
+ * caller.  A call that uses the scratch (more than 2048 rows) clears its
+ * merge tickets on `stream` before its launch; the scratch's device error
+ * word is kept across calls until nwd_noalloc_check reads it.  No
+ * counterpart in the reference. */
 int nwd_attn_decode_noalloc(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
                             uint16_t* o, uint32_t n_heads, uint32_t n_kv_heads,
                             uint32_t head_dim, uint32_t seq, uint32_t cap, float scale,
                             void* stream);
+
+/* Reads (synchronously, on `stream`) and clears the device error word of the
+ * built-in scratch of nwd_attn_decode_noalloc on the current device: 0 = no
+ * error since the last check, else NWD_DEVERR_* bits (a bounded wait that
+ * gave up, a row outside the cache).  The counterpart of nwd_workspace_check
+ * for callers without a workspace; allocates nothing. */
+int nwd_noalloc_check(uint32_t* device_error, void* stream);
 
 /* One engine attention step (engine/runtime.js:389-391 with the uniforms of
  * :451-452): writes k_new/v_new ([n_kv_heads, head_dim]) into row `seq` of the
@@ -216,6 +225,97 @@ int nwd_attn_merge(const float* part_o, const float* part_ml, uint16_t* o, uint3
  * shards.  No counterpart in the reference (it has no multi-device code). */
 int nwd_attn_merge_packed(const float* packed, uint16_t* o, uint32_t shards, uint32_t batch,
                           uint32_t n_heads, uint32_t head_dim, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* Long contexts sharded across GPUs (NCCL over NVLink)                */
+/* ------------------------------------------------------------------ */
+
+/* One process (or thread) per GPU.  Each sequence's cached rows are split into
+ * contiguous shards, one per rank; a step computes every rank's shard partial
+ * (nwd_attn_decode_partial), all-gathers the packed partials with NCCL and
+ * merges them in rank order (nwd_attn_merge_packed), so every rank ends with
+ * the full O.  The reference has no multi-device code: this extends its
+ * single-sequence attention (kernels/sparse_attn.wgsl:32-113, dispatched at
+ * engine/runtime.js:391) to rows held by several GPUs.
+ *
+ * NCCL is loaded at run time on the first nwd_mgpu_* call (NWD_NCCL_LIBRARY,
+ * else libnccl.so.2 as the process finds it).  Communicators are
+ * non-blocking: every wait (set-up, enqueue, step completion, finalize) runs
+ * under a host-side deadline; when it passes, or NCCL reports an error, the
+ * communicator is aborted (ncclCommAbort ends its kernels), the call returns
+ * NWD_ERR_TIMEOUT or NWD_ERR_NCCL and the handle only accepts
+ * nwd_mgpu_destroy / nwd_mgpu_abort.  This is how a rank learns that a peer
+ * left: its next step's wait runs out instead of hanging (the reference's
+ * counterpart is WebGPU device loss, engine/runtime.js:474-487, :700-715). */
+
+#define NWD_MGPU_ID_BYTES 128
+typedef struct nwd_mgpu nwd_mgpu;
+
+/* A new communicator id (on one rank; every rank passes the same bytes to
+ * nwd_mgpu_init). */
+int nwd_mgpu_unique_id(uint8_t* id /* [NWD_MGPU_ID_BYTES] */);
+
+/* Joins the communicator as `rank` of `world` on `device` (made current).
+ * init_deadline_ms bounds the set-up (all ranks must join within it);
+ * step_deadline_ms bounds every later wait. */
+int nwd_mgpu_init(const uint8_t* id, int world, int rank, int device, uint32_t init_deadline_ms,
+                  uint32_t step_deadline_ms, nwd_mgpu** out);
+
+/* Workspace bytes for nwd_mgpu_decode_step on the current device: the shard
+ * partial's workspace plus the gathered partials ([world][batch * n_heads *
+ * (head_dim + 2)] f32).  Zero it once (nwd_workspace_init); 256-byte aligned. */
+int nwd_mgpu_workspace_size(int world, uint32_t batch, uint32_t n_heads, uint32_t n_kv_heads,
+                            uint32_t head_dim, size_t* bytes);
+
+/* One sharded step, asynchronous on `stream`: this rank's rows of sequence b
+ * are pool rows [row_offset[b], row_offset[b] + seq_len[b]) (device arrays,
+ * as nwd_attn_decode_partial); q [batch, n_heads, head_dim] must be the same
+ * on every rank; every rank receives o [batch, n_heads, head_dim] fp16.  All
+ * ranks must make the same calls in the same order.  Returns once the step is
+ * enqueued (or the enqueue's wait ran out); nwd_mgpu_sync waits for it. */
+int nwd_mgpu_decode_step(nwd_mgpu* m, const uint16_t* q, const uint16_t* k_pool,
+                         const uint16_t* v_pool, uint64_t pool_rows, const int64_t* row_offset,
+                         const int32_t* seq_len, uint16_t* o, uint32_t batch, uint32_t n_heads,
+                         uint32_t n_kv_heads, uint32_t head_dim, float scale, void* workspace,
+                         size_t ws_bytes, void* stream);
+
+/* Waits (polling, within step_deadline_ms) for the last step enqueued on this
+ * handle.  On a deadline or an NCCL error it aborts the communicator, lets
+ * the stream drain and returns NWD_ERR_TIMEOUT / NWD_ERR_NCCL. */
+int nwd_mgpu_sync(nwd_mgpu* m);
+
+/* Per-step device timing (CUDA events around the shard partial and around
+ * the all-gather + merge), off by default. */
+int nwd_mgpu_set_timing(nwd_mgpu* m, int on);
+int nwd_mgpu_step_times(nwd_mgpu* m, float* partial_ms, float* exchange_ms);
+
+/* Finalizes (within step_deadline_ms; aborts if that runs out) and frees. */
+int nwd_mgpu_destroy(nwd_mgpu* m);
+/* Aborts without waiting for peers (a rank leaving) and frees. */
+int nwd_mgpu_abort(nwd_mgpu* m);
+/* The loaded NCCL's version code (e.g. 22809). */
+int nwd_mgpu_nccl_version(int* version);
+
+/* ------------------------------------------------------------------ */
+/* Device memory and streams for hosts without a CUDA runtime          */
+/* ------------------------------------------------------------------ */
+
+/* The addon's (or a C engine's) buffer and queue helpers, in place of the
+ * reference's WebGPU helpers (kernels/gpu.js:75-99 createBuffer /
+ * createEmptyStorage / createUniform, :141 dispatchAndRead). */
+int nwd_set_device(int device);
+int nwd_device_count(int* count);
+/* Zero-filled device memory (256-byte aligned, as every workspace needs). */
+int nwd_alloc(size_t bytes, void** ptr);
+int nwd_free(void* ptr);
+/* Asynchronous on `stream`; a pinned `src` must stay unchanged until the
+ * stream has passed the copy, a pageable one may be reused on return. */
+int nwd_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream);
+/* Returns once `dst` holds the data (the stream is synchronised). */
+int nwd_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream);
+int nwd_stream_create(void** stream);
+int nwd_stream_destroy(void* stream);
+int nwd_stream_synchronize(void* stream);
 
 /* ------------------------------------------------------------------ */
 /* The q4 projections either side of the path                          */

@@ -58,6 +58,7 @@ SIGNATURES = {
                                        _sz, _P]),
     "nwd_attn_decode_noalloc": (ctypes.c_int, [_P, _P, _P, _P, _u32, _u32, _u32, _u32, _u32,
                                                _f32, _P]),
+    "nwd_noalloc_check": (ctypes.c_int, [ctypes.POINTER(_u32), _P]),
     "nwd_kv_append_attn_decode": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _u32, _u32, _u32, _u32,
                                                  _u32, _f32, _P, _sz, _P]),
     "nwd_attn_decode_batched": (ctypes.c_int, [_P, _P, _P, _u64, _P, _P, _P, _u32, _u32, _u32,
@@ -80,6 +81,28 @@ SIGNATURES = {
                                           _P, _sz, _P]),
     "nwd_attn_prefill": (ctypes.c_int, [_P, _P, _P, _u64, _P, _P, _u32, _u32, _u32, _u32, _u32,
                                         _u32, _f32, _P, _sz, _P]),
+    "nwd_mgpu_unique_id": (ctypes.c_int, [_P]),
+    "nwd_mgpu_init": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _u32, _u32,
+                                     ctypes.POINTER(_P)]),
+    "nwd_mgpu_workspace_size": (ctypes.c_int, [ctypes.c_int, _u32, _u32, _u32, _u32,
+                                               ctypes.POINTER(_sz)]),
+    "nwd_mgpu_decode_step": (ctypes.c_int, [_P, _P, _P, _P, _u64, _P, _P, _P, _u32, _u32, _u32,
+                                            _u32, _f32, _P, _sz, _P]),
+    "nwd_mgpu_sync": (ctypes.c_int, [_P]),
+    "nwd_mgpu_set_timing": (ctypes.c_int, [_P, ctypes.c_int]),
+    "nwd_mgpu_step_times": (ctypes.c_int, [_P, ctypes.POINTER(_f32), ctypes.POINTER(_f32)]),
+    "nwd_mgpu_destroy": (ctypes.c_int, [_P]),
+    "nwd_mgpu_abort": (ctypes.c_int, [_P]),
+    "nwd_mgpu_nccl_version": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "nwd_set_device": (ctypes.c_int, [ctypes.c_int]),
+    "nwd_device_count": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "nwd_alloc": (ctypes.c_int, [_sz, ctypes.POINTER(_P)]),
+    "nwd_free": (ctypes.c_int, [_P]),
+    "nwd_memcpy_h2d": (ctypes.c_int, [_P, _P, _sz, _P]),
+    "nwd_memcpy_d2h": (ctypes.c_int, [_P, _P, _sz, _P]),
+    "nwd_stream_create": (ctypes.c_int, [ctypes.POINTER(_P)]),
+    "nwd_stream_destroy": (ctypes.c_int, [_P]),
+    "nwd_stream_synchronize": (ctypes.c_int, [_P]),
 }
 
 _lib = None

@@ -20,6 +20,8 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 INCLUDE = os.path.join(REPO_DIR, "include")
 BUILD_DIR = os.path.join(PKG_DIR, "_build")
 LIB_PATH = os.path.join(PKG_DIR, "libnwd.so")
+HOST_SRC = os.path.join(PKG_DIR, "host", "nwd_host.cc")
+HOST_PATH = os.path.join(PKG_DIR, "nwd_host")
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH_FLAGS + [
@@ -70,7 +72,22 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
         os.replace(tmp, LIB_PATH)
+    build_host(verbose)
     return LIB_PATH
+
+
+def build_host(verbose: bool = False) -> str:
+    """The C++ engine host (host/nwd_host.cc): links only libnwd.so, found next to it."""
+    if _stale(HOST_PATH, [HOST_SRC, LIB_PATH, os.path.join(INCLUDE, "nwd.h")]):
+        cxx = os.environ.get("CXX_HOST", "g++")
+        tmp = HOST_PATH + ".tmp"
+        cmd = [cxx, "-O2", "-std=c++17", "-Wall", "-Wextra", "-I", INCLUDE, HOST_SRC, "-o", tmp,
+               "-L", PKG_DIR, "-lnwd", "-Wl,-rpath,$ORIGIN"]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+        os.replace(tmp, HOST_PATH)
+    return HOST_PATH
 
 
 if __name__ == "__main__":

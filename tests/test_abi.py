@@ -98,3 +98,45 @@ def test_prefetch_argument_errors_before_launch(nwd):
     assert lib.nwd_prefetch_l2(None, None, 0, None) == _lib.NWD_OK
     empty = (ctypes.c_uint64 * 1)(0)
     assert lib.nwd_prefetch_l2(null, empty, 1, None) == _lib.NWD_OK
+
+
+def test_mgpu_entry_points_before_any_device(nwd):
+    """The multi-GPU entry points load NCCL at run time: a communicator id is made
+    without a GPU, and argument errors come back before any CUDA or NCCL call."""
+    from importlib import import_module
+    _lib = import_module(nwd.__name__ + "._lib")
+    lib = _lib.load()
+    uid = (ctypes.c_uint8 * 128)()
+    assert lib.nwd_mgpu_unique_id(uid) == _lib.NWD_OK, lib.nwd_last_error()
+    assert any(bytes(uid))
+    ver = ctypes.c_int(0)
+    assert lib.nwd_mgpu_nccl_version(ctypes.byref(ver)) == _lib.NWD_OK
+    assert ver.value >= 21400  # ncclCommInitRankConfig and non-blocking communicators
+    h = ctypes.c_void_p()
+    assert lib.nwd_mgpu_init(uid, 2, 2, 0, 1000, 1000, ctypes.byref(h)) == _lib.NWD_ERR_INVALID
+    assert b"rank 2 outside world 2" in lib.nwd_last_error()
+    assert lib.nwd_mgpu_init(uid, 2, 0, 0, 0, 1000, ctypes.byref(h)) == _lib.NWD_ERR_INVALID
+    assert lib.nwd_mgpu_init(None, 2, 0, 0, 1, 1, ctypes.byref(h)) == _lib.NWD_ERR_INVALID
+    assert lib.nwd_mgpu_sync(None) == _lib.NWD_ERR_INVALID
+    assert lib.nwd_mgpu_destroy(None) == _lib.NWD_OK
+    assert lib.nwd_mgpu_workspace_size(0, 1, 32, 8, 128, ctypes.byref(ctypes.c_size_t())) == \
+        _lib.NWD_ERR_INVALID
+    p = ctypes.c_void_p(1)
+    assert lib.nwd_alloc(0, ctypes.byref(p)) == _lib.NWD_OK and not p.value
+    assert lib.nwd_free(None) == _lib.NWD_OK
+    assert lib.nwd_memcpy_h2d(None, None, 16, None) == _lib.NWD_ERR_INVALID
+
+
+def test_cpp_host_links_only_the_library(nwd):
+    """nwd_host (the C++ engine host) needs libnwd.so and the C/C++ runtime only: no
+    Python, no PyTorch, no separate CUDA runtime."""
+    import os
+    import subprocess
+    pkg = os.path.dirname(nwd.__file__)
+    host = os.path.join(pkg, "nwd_host")
+    assert os.path.exists(host)
+    deps = subprocess.run(["ldd", host], capture_output=True, text=True).stdout
+    assert os.path.join(pkg, "libnwd.so") in deps
+    assert "torch" not in deps and "python" not in deps and "libcudart" not in deps
+    p = subprocess.run([host], capture_output=True, text=True)
+    assert p.returncode == 2 and "usage" in p.stderr
