@@ -18,10 +18,19 @@
 //                   {seq, cap, K, n_heads, n_kv_heads, head_dim})
 //       the q/k/v GEMVs and both kv_append dispatches of runtime.js:385-390
 //   nwd.alloc(bytes) / nwd.upload(buf, typedArray) / nwd.download(buf, typedArray)
+//       device buffers through the library's own helpers (nwd_alloc,
+//       nwd_memcpy_*), in place of kernels/gpu.js:75-99 / :141; the addon
+//       needs no CUDA runtime of its own
+//   nwd.mgpuUniqueId() -> Buffer(128)
+//   nwd.mgpuInit(id, {world, rank, device, init_deadline_ms, step_deadline_ms})
+//   nwd.mgpuDecodeStep(comm, q, kPool, vPool, rowOffset, seqLen, o,
+//                      {batch, n_heads, n_kv_heads, head_dim, pool_rows})
+//   nwd.mgpuSync(comm) / nwd.mgpuDestroy(comm)
+//       the long-context step sharded across GPUs (nwd_mgpu_*): one process
+//       per GPU; rank 0's id reaches the other processes by any channel
 // Buffers are napi_external wrappers of device pointers, freed when the
 // wrapper is garbage-collected.  A non-zero status
 // throws Error(nwd_last_error()), as runtime.js throws on errors (:448, :484).
-#include <cuda_runtime.h>
 #include <node_api.h>
 
 #include <cstdint>
@@ -44,7 +53,7 @@ napi_value throw_status(napi_env env, int status) {
 
 void finalize_buf(napi_env, void* data, void*) {
   auto* b = static_cast<DevBuf*>(data);
-  if (b->ptr) cudaFree(b->ptr);
+  if (b->ptr) nwd_free(b->ptr);
   delete b;
 }
 
@@ -85,10 +94,9 @@ int ensure_ws(uint32_t nh, uint32_t nkv, uint32_t hd) {
   size_t bytes = 0;
   int st = nwd_attn_decode_workspace_size(1, nh, nkv, hd, &bytes);
   if (st) return st;
-  if (g_ws.ptr) cudaFree(g_ws.ptr);
+  if (g_ws.ptr) nwd_free(g_ws.ptr);
   g_ws = Workspace{};
-  if (cudaMalloc(&g_ws.ptr, bytes) != cudaSuccess) return NWD_ERR_CUDA;
-  st = nwd_workspace_init(g_ws.ptr, bytes, nullptr);
+  st = nwd_alloc(bytes, &g_ws.ptr);  // zero-filled: ready for its first use
   if (st) return st;
   g_ws.bytes = bytes;
   g_ws.nh = nh;
@@ -104,10 +112,10 @@ napi_value Alloc(napi_env env, napi_callback_info info) {
   int64_t bytes = 0;
   napi_get_value_int64(env, argv[0], &bytes);
   auto* b = new DevBuf{nullptr, (size_t)bytes};
-  if (cudaMalloc(&b->ptr, b->bytes) != cudaSuccess || cudaMemset(b->ptr, 0, b->bytes) != cudaSuccess) {
+  int st = nwd_alloc(b->bytes, &b->ptr);
+  if (st) {
     delete b;
-    napi_throw_error(env, nullptr, "cudaMalloc failed");
-    return nullptr;
+    return throw_status(env, st);
   }
   napi_value out;
   napi_create_external(env, b, finalize_buf, nullptr, &out);
@@ -134,13 +142,12 @@ napi_value Copy(napi_env env, napi_callback_info info, bool upload) {
     napi_throw_range_error(env, nullptr, "typed array larger than the device buffer");
     return nullptr;
   }
-  cudaError_t e = upload ? cudaMemcpy(b->ptr, data, bytes, cudaMemcpyHostToDevice)
-                         : cudaMemcpy(data, b->ptr, bytes, cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) {
-    napi_throw_error(env, nullptr, cudaGetErrorString(e));
-    return nullptr;
-  }
-  return nullptr;
+  // pageable JS memory: the upload returns once the data is staged, the
+  // download once it has landed (legacy default stream, ordered after the
+  // engine's launches)
+  int st = upload ? nwd_memcpy_h2d(b->ptr, data, bytes, nullptr)
+                  : nwd_memcpy_d2h(data, b->ptr, bytes, nullptr);
+  return st ? throw_status(env, st) : nullptr;
 }
 napi_value Upload(napi_env env, napi_callback_info info) { return Copy(env, info, true); }
 napi_value Download(napi_env env, napi_callback_info info) { return Copy(env, info, false); }
@@ -257,6 +264,120 @@ napi_value Q4QkvAppend(napi_env env, napi_callback_info info) {
   return st ? throw_status(env, st) : nullptr;
 }
 
+// ---- long contexts sharded across GPUs (nwd_mgpu_*) ----
+struct Comm {
+  nwd_mgpu* m = nullptr;
+  DevBuf ws{nullptr, 0};
+  uint32_t batch = 0, nh = 0, nkv = 0, hd = 0;
+  int world = 0;
+};
+
+void finalize_comm(napi_env, void* data, void*) {
+  auto* c = static_cast<Comm*>(data);
+  if (c->m) nwd_mgpu_destroy(c->m);
+  if (c->ws.ptr) nwd_free(c->ws.ptr);
+  delete c;
+}
+
+napi_value MgpuUniqueId(napi_env env, napi_callback_info) {
+  uint8_t id[NWD_MGPU_ID_BYTES];
+  int st = nwd_mgpu_unique_id(id);
+  if (st) return throw_status(env, st);
+  napi_value out;
+  void* data = nullptr;
+  napi_create_buffer_copy(env, sizeof(id), id, &data, &out);
+  return out;
+}
+
+napi_value MgpuInit(napi_env env, napi_callback_info info) {
+  size_t argc = 2;
+  napi_value argv[2];
+  napi_get_cb_info(env, info, &argc, argv, nullptr, nullptr);
+  void* id = nullptr;
+  size_t len = 0;
+  if (napi_get_buffer_info(env, argv[0], &id, &len) != napi_ok || len != NWD_MGPU_ID_BYTES) {
+    napi_throw_type_error(env, nullptr, "expected the 128-byte id from mgpuUniqueId");
+    return nullptr;
+  }
+  auto* c = new Comm;
+  c->world = (int)get_u32(env, argv[1], "world");
+  const int rank = (int)get_u32(env, argv[1], "rank");
+  const int device = (int)get_u32(env, argv[1], "device", (uint32_t)rank, false);
+  const uint32_t init_ms = get_u32(env, argv[1], "init_deadline_ms", 120000, false);
+  const uint32_t step_ms = get_u32(env, argv[1], "step_deadline_ms", 60000, false);
+  int st = nwd_mgpu_init(static_cast<const uint8_t*>(id), c->world, rank, device, init_ms, step_ms,
+                         &c->m);
+  if (st) {
+    delete c;
+    return throw_status(env, st);
+  }
+  napi_value out;
+  napi_create_external(env, c, finalize_comm, nullptr, &out);
+  return out;
+}
+
+Comm* get_comm(napi_env env, napi_value v) {
+  void* data = nullptr;
+  if (napi_get_value_external(env, v, &data) != napi_ok || !data) {
+    napi_throw_type_error(env, nullptr, "expected a communicator from mgpuInit");
+    return nullptr;
+  }
+  return static_cast<Comm*>(data);
+}
+
+napi_value MgpuDecodeStep(napi_env env, napi_callback_info info) {
+  size_t argc = 8;
+  napi_value argv[8];
+  napi_get_cb_info(env, info, &argc, argv, nullptr, nullptr);
+  Comm* c = get_comm(env, argv[0]);
+  DevBuf *q = get_buf(env, argv[1]), *k = get_buf(env, argv[2]), *v = get_buf(env, argv[3]),
+         *ro = get_buf(env, argv[4]), *sl = get_buf(env, argv[5]), *o = get_buf(env, argv[6]);
+  if (!c || !q || !k || !v || !ro || !sl || !o) return nullptr;
+  const uint32_t batch = get_u32(env, argv[7], "batch"), nh = get_u32(env, argv[7], "n_heads"),
+                 nkv = get_u32(env, argv[7], "n_kv_heads"), hd = get_u32(env, argv[7], "head_dim");
+  const uint64_t rows = get_u32(env, argv[7], "pool_rows", (uint32_t)(k->bytes / (2ull * nkv * hd)),
+                                false);
+  if (!c->ws.ptr || c->batch != batch || c->nh != nh || c->nkv != nkv || c->hd != hd) {
+    size_t bytes = 0;
+    int st = nwd_mgpu_workspace_size(c->world, batch, nh, nkv, hd, &bytes);
+    if (!st && c->ws.ptr) st = nwd_free(c->ws.ptr);
+    c->ws = DevBuf{nullptr, 0};
+    if (!st) st = nwd_alloc(bytes, &c->ws.ptr);  // zero-filled
+    if (st) return throw_status(env, st);
+    c->ws.bytes = bytes;
+    c->batch = batch;
+    c->nh = nh;
+    c->nkv = nkv;
+    c->hd = hd;
+  }
+  int st = nwd_mgpu_decode_step(c->m, (const uint16_t*)q->ptr, (const uint16_t*)k->ptr,
+                                (const uint16_t*)v->ptr, rows, (const int64_t*)ro->ptr,
+                                (const int32_t*)sl->ptr, (uint16_t*)o->ptr, batch, nh, nkv, hd,
+                                0.0f, c->ws.ptr, c->ws.bytes, nullptr);
+  return st ? throw_status(env, st) : nullptr;
+}
+
+napi_value MgpuSync(napi_env env, napi_callback_info info) {
+  size_t argc = 1;
+  napi_value argv[1];
+  napi_get_cb_info(env, info, &argc, argv, nullptr, nullptr);
+  Comm* c = get_comm(env, argv[0]);
+  if (!c) return nullptr;
+  int st = nwd_mgpu_sync(c->m);
+  return st ? throw_status(env, st) : nullptr;
+}
+
+napi_value MgpuDestroy(napi_env env, napi_callback_info info) {
+  size_t argc = 1;
+  napi_value argv[1];
+  napi_get_cb_info(env, info, &argc, argv, nullptr, nullptr);
+  Comm* c = get_comm(env, argv[0]);
+  if (!c) return nullptr;
+  int st = nwd_mgpu_destroy(c->m);
+  c->m = nullptr;  // the finalizer frees the rest
+  return st ? throw_status(env, st) : nullptr;
+}
+
 napi_value Init(napi_env env, napi_value exports) {
   napi_property_descriptor props[] = {
       {"alloc", nullptr, Alloc, nullptr, nullptr, nullptr, napi_default, nullptr},
@@ -268,6 +389,12 @@ napi_value Init(napi_env env, napi_value exports) {
        nullptr},
       {"q4Gemv", nullptr, Q4Gemv, nullptr, nullptr, nullptr, napi_default, nullptr},
       {"q4QkvAppend", nullptr, Q4QkvAppend, nullptr, nullptr, nullptr, napi_default, nullptr},
+      {"mgpuUniqueId", nullptr, MgpuUniqueId, nullptr, nullptr, nullptr, napi_default, nullptr},
+      {"mgpuInit", nullptr, MgpuInit, nullptr, nullptr, nullptr, napi_default, nullptr},
+      {"mgpuDecodeStep", nullptr, MgpuDecodeStep, nullptr, nullptr, nullptr, napi_default,
+       nullptr},
+      {"mgpuSync", nullptr, MgpuSync, nullptr, nullptr, nullptr, napi_default, nullptr},
+      {"mgpuDestroy", nullptr, MgpuDestroy, nullptr, nullptr, nullptr, napi_default, nullptr},
   };
   napi_define_properties(env, exports, sizeof(props) / sizeof(props[0]), props);
   return exports;

@@ -25,6 +25,8 @@ napi_status napi_get_value_int64(napi_env, napi_value, int64_t*);
 napi_status napi_get_cb_info(napi_env, napi_callback_info, size_t*, napi_value*, napi_value*, void**);
 napi_status napi_create_external(napi_env, void*, napi_finalize, void*, napi_value*);
 napi_status napi_get_typedarray_info(napi_env, napi_value, napi_typedarray_type*, size_t*, void**, napi_value*, size_t*);
+napi_status napi_create_buffer_copy(napi_env, size_t, const void*, void**, napi_value*);
+napi_status napi_get_buffer_info(napi_env, napi_value, void**, size_t*);
 napi_status napi_define_properties(napi_env, napi_value, size_t, const napi_property_descriptor*);
 #define NODE_GYP_MODULE_NAME nwd
 #define NAPI_MODULE(name, init) extern "C" napi_value nwd_napi_init(napi_env e, napi_value x) { return init(e, x); }

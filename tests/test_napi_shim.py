@@ -16,10 +16,10 @@ SHIM = os.path.join(REPO, "nemotron-webgpu-decode_b200", "napi", "nwd_napi.cc")
 
 @pytest.mark.skipif(shutil.which("g++") is None, reason="g++ not installed")
 def test_shim_compiles(tmp_path):
-    cuda_inc = "/usr/local/cuda/include"
+    # no CUDA include path: the addon reaches the GPU only through include/nwd.h
     cmd = ["g++", "-std=c++17", "-fsyntax-only", "-Wall", "-Werror",
            "-I", os.path.join(REPO, "tests", "napi_stub"), "-I", os.path.join(REPO, "include"),
-           "-I", cuda_inc, SHIM]
+           SHIM]
     r = subprocess.run(cmd, capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
 
