@@ -162,6 +162,19 @@ int nwd_attn_decode_noalloc(const uint16_t* q, const uint16_t* k_cache, const ui
  * for callers without a workspace; allocates nothing. */
 int nwd_noalloc_check(uint32_t* device_error, void* stream);
 
+/* How a decode call of this shape runs on the current device, without
+ * launching anything: batch 1 plans nwd_attn_decode of `seq` rows (and the
+ * fused step attending `seq` rows), batch > 1 the batched entry points
+ * (`seq` is ignored).  kernel: 0 = the split-KV kernel, 1 = the short
+ * single-sequence kernel; grid: CTAs; split: pieces per kv head of a single
+ * sequence (0 = the batch's flattened split); cluster: CTAs per thread-block
+ * cluster whose pieces merge over distributed shared memory (0 = none);
+ * groups: consumer warp groups of the split-KV kernel.  No counterpart in the
+ * reference (its attention is one fixed dispatch, engine/runtime.js:391). */
+int nwd_attn_decode_plan(uint32_t batch, uint32_t n_heads, uint32_t n_kv_heads,
+                         uint32_t head_dim, uint32_t seq, int* kernel, int* grid, int* split,
+                         int* cluster, int* groups);
+
 /* One engine attention step (engine/runtime.js:389-391 with the uniforms of
  * :451-452): writes k_new/v_new ([n_kv_heads, head_dim]) into row `seq` of the
  * caches, then attends over rows 0..seq (seq + 1 rows), in one launch. */

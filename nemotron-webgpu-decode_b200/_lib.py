@@ -59,6 +59,8 @@ SIGNATURES = {
     "nwd_attn_decode_noalloc": (ctypes.c_int, [_P, _P, _P, _P, _u32, _u32, _u32, _u32, _u32,
                                                _f32, _P]),
     "nwd_noalloc_check": (ctypes.c_int, [ctypes.POINTER(_u32), _P]),
+    "nwd_attn_decode_plan": (ctypes.c_int, [_u32, _u32, _u32, _u32, _u32] +
+                             [ctypes.POINTER(ctypes.c_int)] * 5),
     "nwd_kv_append_attn_decode": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _u32, _u32, _u32, _u32,
                                                  _u32, _f32, _P, _sz, _P]),
     "nwd_attn_decode_batched": (ctypes.c_int, [_P, _P, _P, _u64, _P, _P, _P, _u32, _u32, _u32,

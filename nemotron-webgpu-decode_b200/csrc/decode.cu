@@ -93,6 +93,8 @@ struct Params {
   uint32_t pair_max;   // one CTA per (sequence, kv head) when every pair is this short
   uint32_t split_k;    // > 0: CTA i takes piece i % k of pair i / k (k equal pieces per pair)
   uint32_t prefetch;   // single sequence: K/V tiles per CTA prefetched into L2 before the wait
+  uint32_t cluster;    // > 0: launched as clusters of this many CTAs, one cluster per kv
+                       // head (split_k == cluster); the pieces merge over DSMEM
 };
 
 // ---- shared memory layout (offsets from a 1024-aligned base) ----
@@ -172,6 +174,37 @@ __device__ __forceinline__ bool consumer_sync(uint32_t bar, uint32_t& ph, volati
   const bool ok = warp_wait(bar, ph, abort, dev_err);
   ph ^= 1u;
   return ok;
+}
+
+// Cluster-wide barrier over every thread of every CTA of the cluster (release
+// / acquire: shared-memory writes before it are visible to the cluster's
+// distributed-shared-memory loads after it).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// Loads from CTA `rank`'s shared memory at the offset `local` has in this CTA.
+__device__ __forceinline__ uint32_t cluster_addr(const void* local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+               : "=r"(remote)
+               : "r"(smem_u32(local)), "r"(rank));
+  return remote;
+}
+__device__ __forceinline__ float2 ld_cluster_f2(const float* local, uint32_t rank) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];"
+               : "=f"(v.x), "=f"(v.y)
+               : "r"(cluster_addr(local, rank))
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 ld_cluster_f4(const float* local, uint32_t rank) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr(local, rank))
+               : "memory");
+  return v;
 }
 
 // Byte offset of 16-byte chunk `chunk16` of 128-byte row R inside a stage
@@ -391,34 +424,64 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
     bool aborted = false;
 
     // emits one piece: rows [t0, t1) of pair (b, hkv)
+    // fused kv_append: the new row L-1 of kv head hkv of sequence b (lanes
+    // 0-15: K, 16-31: V), written with generic stores; the TMA load of the
+    // tile holding it must come after a proxy fence by the same lanes.  Any
+    // wait in this warp stops this SM's stream, so the row's load is issued
+    // one piece ahead, stored once the piece before has issued its stages,
+    // and the fence sits just before the one tile that reads the row.
+    struct PendRow {
+      uint4 v;
+      uint4* dst;
+      bool valid, stored;
+    };
+    auto load_row = [&](uint32_t b, uint32_t hkv, uint32_t L, PendRow& r) {
+      r.valid = r.stored = false;
+      const int64_t row = seq_off(p, b) + (int64_t)L - 1;
+      if (row >= 0 && (uint64_t)row < p.pool_rows) {
+        const size_t dst = ((size_t)row * p.n_kv + hkv) * HD;
+        const size_t src = ((size_t)b * p.n_kv + hkv) * HD;
+        const int half = lane >> 4, j = lane & 15;
+        r.dst = reinterpret_cast<uint4*>((half ? p.v_pool : p.k_pool) + dst) + j;
+        r.v = __ldg(reinterpret_cast<const uint4*>((half ? p.v_new : p.k_new) + src) + j);
+        r.valid = true;
+      } else if (lane == 0) {
+        atomicOr(&wsh->error, NWD_DEVERR_ROW_RANGE);
+      }
+    };
+    auto store_row = [&](PendRow& r) {
+      if (r.valid && !r.stored) {
+        *r.dst = r.v;
+        r.stored = true;
+      }
+    };
+
+    // emits one piece: rows [t0, t1) of pair (b, hkv).  own: this piece's new
+    // row (append mode, t1 == L), possibly loaded and stored by the piece
+    // before; next: the next piece's new row (nb >= 0), loaded here and
+    // stored after this piece's stages.
     auto emit_piece = [&](uint32_t b, uint32_t hkv, uint32_t L, uint32_t t0, uint32_t t1,
-                          bool complete, int32_t f, int32_t l) {
+                          bool complete, int32_t f, int32_t l, PendRow& own, int32_t nb,
+                          uint32_t nhkv, uint32_t nL, PendRow& next) {
       const int32_t pslot = (int32_t)(2u * blockIdx.x + (t0 > 0 ? 0u : 1u));
       const int64_t off = seq_off(p, b);
       if (lane == 0 && t0 == 0 && hkv == 0 && (off < 0 || (uint64_t)off + L > p.pool_rows))
         atomicOr(&wsh->error, NWD_DEVERR_ROW_RANGE);
-      if (p.append && t1 == L) {
-        // fused kv_append: this piece ends at the new row L-1 of kv head hkv
-        const int64_t row = off + (int64_t)L - 1;
-        if (row >= 0 && (uint64_t)row < p.pool_rows) {
-          const size_t dst = ((size_t)row * p.n_kv + hkv) * HD;
-          const size_t src = ((size_t)b * p.n_kv + hkv) * HD;
-          const int half = lane >> 4, j = lane & 15;  // lanes 0-15: K, 16-31: V
-          const uint4* sp = reinterpret_cast<const uint4*>((half ? p.v_new : p.k_new) + src) + j;
-          uint4* dp = reinterpret_cast<uint4*>((half ? p.v_pool : p.k_pool) + dst) + j;
-          *dp = __ldg(sp);
-          asm volatile("fence.proxy.async;" ::: "memory");
-        } else if (lane == 0) {
-          atomicOr(&wsh->error, NWD_DEVERR_ROW_RANGE);
-        }
-        __syncwarp();
-      }
+      const bool ends = p.append && t1 == L;
+      if (ends && !own.valid) load_row(b, hkv, L, own);
+      if (nb >= 0) load_row((uint32_t)nb, nhkv, nL, next);
       const uint32_t nreal = cdiv(t1 - t0, TOK);
       const uint32_t nstages = (nreal + NGRP - 1u) / NGRP * NGRP;
       for (uint32_t s = 0; s < nstages && !aborted; s++) {
         if (!warp_wait(bar_empty + 8 * slot, phase ^ 1u, abort_flag, &wsh->error)) {
           aborted = true;
           break;
+        }
+        if (ends && s + 1 == nreal) {
+          // the tile holding row L-1: the row's stores first, then the fence
+          store_row(own);
+          asm volatile("fence.proxy.async;" ::: "memory");
+          __syncwarp();
         }
         if (lane == 0) {
           StageHdr h;
@@ -453,6 +516,7 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
           phase ^= 1u;
         }
       }
+      if (nb >= 0) store_row(next);  // long before the next piece's fence
     };
 
     if (split_k) {
@@ -462,9 +526,10 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
         const uint32_t L = S[b + 1] - S[b];
         const uint32_t t0 = (uint32_t)((uint64_t)j * L / split_k);
         const uint32_t t1 = (uint32_t)((uint64_t)(j + 1) * L / split_k);
+        PendRow own{}, next{};
         if (t1 > t0)
           emit_piece(b, hkv, L, t0, t1, split_k == 1, (int32_t)(pair * split_k),
-                     (int32_t)(pair * split_k + split_k - 1));
+                     (int32_t)(pair * split_k + split_k - 1), own, -1, 0u, 0u, next);
       }
     } else if (x0 < x1) {
       // locate the first piece, then walk pairs forward (no further division
@@ -476,12 +541,34 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
       uint32_t t0 = (uint32_t)(r - (uint64_t)hkv * L);
       uint64_t pstart = x0 - t0;
       int32_t f = (int32_t)udiv64(pstart, W);
+      PendRow cur{}, nxt{};  // this piece's new row (set up by the piece before), the next one's
       for (uint64_t x = x0; x < x1 && !aborted;) {
         const uint64_t len = min((uint64_t)(L - t0), x1 - x);
         const uint32_t t1 = t0 + (uint32_t)len;
         const bool complete = (t0 == 0 && t1 == L);
         const int32_t l = (t1 == L) ? (int32_t)blockIdx.x : (int32_t)udiv64(pstart + L - 1, W);
-        emit_piece(b, hkv, L, t0, t1, complete, f, l);
+        // append mode: the next piece (the next non-empty pair, from its row
+        // 0) ends at its new row if the range holds the whole pair
+        int32_t nb = -1;
+        uint32_t nhkv = 0, nL = 0;
+        if (p.append && x + len < x1) {
+          uint32_t b2 = b, h2 = hkv + 1;
+          if (h2 == p.n_kv) {
+            h2 = 0;
+            do {
+              b2++;
+            } while (b2 + 1 < B && S[b2 + 1] == S[b2]);
+          }
+          const uint32_t L2 = S[b2 + 1] - S[b2];
+          if (L2 > 0 && (uint64_t)L2 <= x1 - (x + len)) {
+            nb = (int32_t)b2;
+            nhkv = h2;
+            nL = L2;
+          }
+        }
+        nxt.valid = nxt.stored = false;
+        emit_piece(b, hkv, L, t0, t1, complete, f, l, cur, nb, nhkv, nL, nxt);
+        cur = nxt;
         x += len;
         if (x >= x1) break;
         // next pair starts inside this range
@@ -527,9 +614,8 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
           }
         }
     }
-    return;
-  }
-
+    if (!p.cluster) return;
+  } else {
   // ======================= consumer warps =======================
   const uint32_t grp = warp / WPG, wig = warp % WPG;  // group; 16-row slice of a stage
   const uint32_t g0 = 2u * (lane & 3);      // this lane's two heads (C/B fragment cols)
@@ -739,6 +825,20 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
     }
     if (!consumer_sync(bar_csync, cph, abort_flag, &wsh->error)) break;  // scratch free again
 
+    if (p.cluster) {
+      // one piece per CTA: keep its (m, l, o) per head in shared memory at the
+      // same offsets in every CTA of the cluster (row g of [GMAX][HD + 4]:
+      // o, then m, l); the cluster merges them after the loop
+      if (g < G) {
+        float* row = mrg + (size_t)g * (HD + 4);
+        float4* dst = reinterpret_cast<float4*>(row + d0);
+#pragma unroll
+        for (int j = 0; j < NV; j++) dst[j] = o4[j];
+        if (d0 == 0) *reinterpret_cast<float2*>(row + HD) = make_float2(M, Ls);
+      }
+      continue;
+    }
+
     const uint32_t b = (uint32_t)h.b, hkv = (uint32_t)h.hkv;
     bool emit = (h.flags & F_COMPLETE) != 0;
     if (!emit) {
@@ -835,6 +935,50 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
       }
     }
   }
+  }  // consumer warps
+
+  if (p.cluster) {
+    // ======== the cluster's pieces meet over distributed shared memory ========
+    // Every thread of every CTA of the cluster (producer warp included) comes
+    // here exactly once, whether its loop ended normally or gave up on a wait
+    // (then the partial is stale, and the workspace's error word says so).
+    // The first barrier publishes each CTA's partial to the cluster; the
+    // second keeps every CTA resident until the others have read it.
+    cluster_sync_all();
+    const uint32_t C = p.cluster, rank = blockIdx.x % C, hkv = blockIdx.x / C;
+    const float* mrg = reinterpret_cast<const float*>(smem + OFF_MRG);
+    for (uint32_t i = rank * NTHR + tid; i < G * (HD / 4); i += C * NTHR) {
+      const uint32_t g = i / (HD / 4), d = (i % (HD / 4)) * 4;
+      const float* row = mrg + (size_t)g * (HD + 4);
+      float2 ml[16];
+      float M = -INFINITY;
+#pragma unroll
+      for (uint32_t c = 0; c < 16; c++) {
+        ml[c] = c < C ? ld_cluster_f2(row + HD, c) : make_float2(-INFINITY, 0.f);
+        M = fmaxf(M, ml[c].x);
+      }
+      float Ls = 0.f;
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+      // pieces in rank order (= row order): deterministic
+#pragma unroll
+      for (uint32_t c = 0; c < 16; c++) {
+        if (c >= C || ml[c].x == -INFINITY) continue;
+        const float w = ex2(ml[c].x - M);
+        const float4 x = ld_cluster_f4(row + d, c);
+        Ls += w * ml[c].y;
+        o.x += w * x.x;
+        o.y += w * x.y;
+        o.z += w * x.z;
+        o.w += w * x.w;
+      }
+      const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+      uint2 v;
+      v.x = pack_half2(o.x * inv, o.y * inv);
+      v.y = pack_half2(o.z * inv, o.w * inv);
+      *reinterpret_cast<uint2*>(p.o + ((size_t)hkv * G + g) * HD + d) = v;
+    }
+    cluster_sync_all();
+  }
 }
 
 // ---------------- host side ----------------
@@ -851,6 +995,17 @@ struct Tuning {
   uint32_t short_rows = 2048;  // single sequence of at most this many rows: decode_short.cu
   uint32_t short_cta_rows = 128;  // past 256 rows: rows per CTA of a kv head's cluster
   uint32_t prefetch = 8;  // single sequence: K/V tiles per CTA prefetched into L2 under PDL
+  // single sequence split into k pieces per kv head: run each kv head's pieces
+  // as one thread-block cluster (at most cluster_max CTAs, 16 needs the
+  // non-portable opt-in) that merges over distributed shared memory; 0 turns
+  // it off.  Up to cluster_rows rows any size whose clusters all fit at once
+  // is taken (the merge it saves outweighs fewer CTAs: 8 kv heads at 4 096
+  // rows, 80 CTAs in clusters of 10 against 128 unclustered, 10.5 against
+  // 11.6 us); above, only one keeping cluster_keep / 8 of the k CTAs (16 384
+  // rows in clusters of 10: 18.2 against 17.8 us, 32 768: 29.5 against 26.0).
+  uint32_t cluster_max = 16;
+  uint32_t cluster_rows = 8192;
+  uint32_t cluster_keep = 7;
 };
 
 uint32_t env_u32(const char* name, uint32_t dflt) {
@@ -876,6 +1031,14 @@ const Tuning& tuning() {
     // 0 turns the prefetch off
     const char* pf = getenv("NWD_DECODE_PREFETCH");
     if (pf && *pf) x.prefetch = (uint32_t)strtoul(pf, nullptr, 10);
+    // 0 turns the cluster merge off
+    const char* cl = getenv("NWD_DECODE_CLUSTER");
+    if (cl && *cl) x.cluster_max = (uint32_t)strtoul(cl, nullptr, 10);
+    if (x.cluster_max > 16) x.cluster_max = 16;
+    x.cluster_rows = env_u32("NWD_DECODE_CLUSTER_ROWS", x.cluster_rows);
+    const char* ck = getenv("NWD_DECODE_CLUSTER_KEEP");
+    if (ck && *ck) x.cluster_keep = (uint32_t)strtoul(ck, nullptr, 10);
+    if (x.cluster_keep > 8) x.cluster_keep = 8;
     return x;
   }();
   return t;
@@ -885,6 +1048,64 @@ const Tuning& tuning() {
 uint32_t slots_for(const nwd::DeviceInfo& di) { return 2u * (uint32_t)di.sm_count; }
 
 bool g_smem_set[64][3] = {};
+
+// Clusters of c CTAs of decode_kernel<NG> that can be resident at once on
+// the current device (cudaOccupancyMaxActiveClusters), cached per device;
+// 0 if the size cannot be launched.
+int g_cluster_fit[64][3][17];
+bool g_cluster_known[64][3][17] = {};
+std::mutex g_cluster_mu;
+
+template <int NG>
+int cluster_fit(int device, uint32_t c, uint32_t n_kv) {
+  std::lock_guard<std::mutex> lk(g_cluster_mu);
+  if (g_cluster_known[device][NG][c]) return g_cluster_fit[device][NG][c];
+  int n = 0;
+  cudaError_t e = cudaSuccess;
+  if (c > 8)
+    e = cudaFuncSetAttribute(decode_kernel<NG>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c * n_kv);
+    cfg.blockDim = dim3(Cfg<NG>::NTHR);
+    cfg.dynamicSmemBytes = Cfg<NG>::SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = c;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaOccupancyMaxActiveClusters(&n, decode_kernel<NG>, &cfg);
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // not launchable at this size: clear the sticky-free error
+    n = 0;
+  }
+  g_cluster_fit[device][NG][c] = n;
+  g_cluster_known[device][NG][c] = true;
+  return n;
+}
+
+template <int NG>
+cudaError_t launch_cluster(uint32_t grid, uint32_t c, cudaStream_t stream, const CUtensorMap& tmk,
+                           const CUtensorMap& tmv, const Params& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(Cfg<NG>::NTHR);
+  cfg.dynamicSmemBytes = Cfg<NG>::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = c;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, decode_kernel<NG>, tmk, tmv, p);
+}
 
 struct Call {
   const uint16_t* q;
@@ -928,6 +1149,85 @@ bool takes_short_path(const Call& c, const Tuning& tu) {
          (uint32_t)c.single_len <= tu.short_rows;
 }
 
+// How a split-KV launch is cut: grid, pieces per kv head of a single
+// sequence (0 = the flattened stream-K split), CTAs per cluster (0 = none),
+// consumer groups.  Sets the kernel's shared-memory attribute on first use.
+struct Plan {
+  uint32_t grid, split_k, cluster, ng;
+};
+
+int plan_split(const Call& c, const nwd::DeviceInfo& di, const Tuning& tu, Plan* out) {
+  using namespace nwd;
+  const uint32_t grid_max = (uint32_t)di.sm_count;
+  // grid: one CTA per SM; for a single sequence (rows known here) one CTA per
+  // kv head when the sequence is short, else only as many CTAs as ranges of
+  // min_chunk items
+  uint32_t grid = grid_max;
+  uint32_t split_k = 0;
+  if (!c.seq_len) {
+    // single sequence: cut each kv head's rows into k equal pieces, one CTA
+    // each (k = 1 for short sequences: no partials), so no CTA straddles two
+    // heads; fall back to the flattened split when there are more kv heads
+    // than SMs
+    const uint64_t rows = (uint64_t)(c.single_len > 0 ? c.single_len : 0);
+    if (c.n_kv <= grid_max) {
+      uint64_t k = 1;
+      if (rows > tu.pair_max) {
+        k = std::min<uint64_t>(grid_max / c.n_kv, (rows + tu.min_chunk - 1) / tu.min_chunk);
+        if (k < 1) k = 1;
+      }
+      split_k = (uint32_t)k;
+      grid = c.n_kv * (uint32_t)k;
+    } else {
+      const uint64_t need = (c.n_kv * rows + tu.min_chunk - 1) / tu.min_chunk;
+      if (need < grid) grid = (uint32_t)need;
+    }
+  }
+  if (grid == 0) grid = 1;
+  // Consumer groups: two (latency hiding) for batched calls and long single
+  // sequences, one for short single sequences (its epilogue is shorter).
+  uint32_t ng = tu.groups;
+  if (ng == 0) ng = (c.seq_len || (uint64_t)c.single_len >= tu.two_group_rows) ? 2u : 1u;
+  if (!g_smem_set[di.device][ng]) {
+    cudaError_t e = ng == 2 ? cudaFuncSetAttribute(decode_kernel<2>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   Cfg<2>::SMEM_BYTES)
+                            : cudaFuncSetAttribute(decode_kernel<1>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   Cfg<1>::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode_kernel)");
+    g_smem_set[di.device][ng] = true;
+  }
+  // A single sequence cut into k >= 2 pieces per kv head (not a shard
+  // partial): each kv head's pieces run as one cluster and merge over
+  // distributed shared memory instead of workspace partials and a ticket.
+  // The largest size (at most k) whose n_kv clusters can all be resident at
+  // once; past cluster_rows rows only if it keeps at least cluster_keep / 8
+  // of the k CTAs per kv head (long sequences stream faster on more CTAs);
+  // none fits, the split stays as it is.
+  uint32_t cluster = 0;
+  if (!c.seq_len && !c.partial && split_k >= 2 && tu.cluster_max >= 2) {
+    const uint32_t keep = (uint64_t)c.single_len <= tu.cluster_rows ? 0u : tu.cluster_keep;
+    uint32_t C = std::min(split_k, tu.cluster_max);
+    while (C >= 2 && 8u * C >= keep * split_k) {
+      const int fit = ng == 2 ? cluster_fit<2>(di.device, C, c.n_kv)
+                              : cluster_fit<1>(di.device, C, c.n_kv);
+      if (fit >= (int)c.n_kv) break;
+      C--;
+    }
+    if (C >= 2 && 8u * C >= keep * split_k) {
+      cluster = C;
+      split_k = C;
+      grid = c.n_kv * C;
+    }
+  }
+  out->grid = grid;
+  out->split_k = split_k;
+  out->cluster = cluster;
+  out->ng = ng;
+  return NWD_OK;
+}
+
 int launch(const Call& c) {
   using namespace nwd;
   int st = check_shape(c.n_heads, c.n_kv, c.hd, c.who);
@@ -949,7 +1249,6 @@ int launch(const Call& c) {
   st = current_device_info(&di);
   if (st) return st;
   const Tuning& tu = tuning();
-  const uint32_t grid_max = (uint32_t)di.sm_count;
   const uint32_t G = c.n_heads / c.n_kv;
   const WsLayout lay = ws_layout(c.batch, c.n_kv, G, c.hd, slots_for(di));
   if (!c.ws) return fail(NWD_ERR_WORKSPACE, "%s: workspace is NULL", c.who);
@@ -1010,50 +1309,21 @@ int launch(const Call& c) {
   p.prefetch = tu.prefetch;
   p.pair_max = tu.pair_max;
 
-  // grid: one CTA per SM; for a single sequence (rows known here) one CTA per
-  // kv head when the sequence is short, else only as many CTAs as ranges of
-  // min_chunk items
-  uint32_t grid = grid_max;
-  p.split_k = 0;
-  if (!c.seq_len) {
-    // single sequence: cut each kv head's rows into k equal pieces, one CTA
-    // each (k = 1 for short sequences: no partials), so no CTA straddles two
-    // heads; fall back to the flattened split when there are more kv heads
-    // than SMs
-    const uint64_t rows = (uint64_t)(c.single_len > 0 ? c.single_len : 0);
-    if (c.n_kv <= grid_max) {
-      uint64_t k = 1;
-      if (rows > tu.pair_max) {
-        k = std::min<uint64_t>(grid_max / c.n_kv, (rows + tu.min_chunk - 1) / tu.min_chunk);
-        if (k < 1) k = 1;
-      }
-      p.split_k = (uint32_t)k;
-      grid = c.n_kv * (uint32_t)k;
-    } else {
-      const uint64_t need = (c.n_kv * rows + tu.min_chunk - 1) / tu.min_chunk;
-      if (need < grid) grid = (uint32_t)need;
-    }
-  }
-  if (grid == 0) grid = 1;
-  // Consumer groups: two (latency hiding) for batched calls and long single
-  // sequences, one for short single sequences (its epilogue is shorter).
-  uint32_t ng = tu.groups;
-  if (ng == 0) ng = (c.seq_len || (uint64_t)c.single_len >= tu.two_group_rows) ? 2u : 1u;
-  if (!g_smem_set[di.device][ng]) {
-    cudaError_t e = ng == 2 ? cudaFuncSetAttribute(decode_kernel<2>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   Cfg<2>::SMEM_BYTES)
-                            : cudaFuncSetAttribute(decode_kernel<1>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   Cfg<1>::SMEM_BYTES);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode_kernel)");
-    g_smem_set[di.device][ng] = true;
-  }
-  cudaError_t e =
-      ng == 2 ? launch_pdl(decode_kernel<2>, dim3(grid), dim3(Cfg<2>::NTHR), Cfg<2>::SMEM_BYTES,
-                           (cudaStream_t)c.stream, tmk, tmv, p)
-              : launch_pdl(decode_kernel<1>, dim3(grid), dim3(Cfg<1>::NTHR), Cfg<1>::SMEM_BYTES,
-                           (cudaStream_t)c.stream, tmk, tmv, p);
+  Plan pl;
+  st = plan_split(c, di, tu, &pl);
+  if (st) return st;
+  p.split_k = pl.split_k;
+  p.cluster = pl.cluster;
+  const uint32_t grid = pl.grid, ng = pl.ng;
+  cudaError_t e;
+  if (p.cluster)
+    e = ng == 2 ? launch_cluster<2>(grid, p.cluster, (cudaStream_t)c.stream, tmk, tmv, p)
+                : launch_cluster<1>(grid, p.cluster, (cudaStream_t)c.stream, tmk, tmv, p);
+  else
+    e = ng == 2 ? launch_pdl(decode_kernel<2>, dim3(grid), dim3(Cfg<2>::NTHR), Cfg<2>::SMEM_BYTES,
+                             (cudaStream_t)c.stream, tmk, tmv, p)
+                : launch_pdl(decode_kernel<1>, dim3(grid), dim3(Cfg<1>::NTHR), Cfg<1>::SMEM_BYTES,
+                             (cudaStream_t)c.stream, tmk, tmv, p);
   if (e != cudaSuccess) return cuda_fail(e, c.who);
   return ok();
 }
@@ -1178,6 +1448,49 @@ int nwd_attn_decode_noalloc(const uint16_t* q, const uint16_t* k_cache, const ui
     if (e != cudaSuccess) return cuda_fail(e, "clearing the decode scratch's merge tickets");
   }
   return launch(c);
+}
+
+int nwd_attn_decode_plan(uint32_t batch, uint32_t n_heads, uint32_t n_kv_heads,
+                         uint32_t head_dim, uint32_t seq, int* kernel, int* grid, int* split,
+                         int* cluster, int* groups) {
+  const char* who = "nwd_attn_decode_plan";
+  if (!kernel || !grid || !split || !cluster || !groups)
+    return fail(NWD_ERR_INVALID, "%s: null pointer", who);
+  int st = check_shape(n_heads, n_kv_heads, head_dim, who);
+  if (st) return st;
+  if (batch == 0 || batch > (uint32_t)MAXB)
+    return fail(NWD_ERR_UNSUPPORTED, "%s: batch %u outside [1, %d]", who, batch, MAXB);
+  DeviceInfo di;
+  st = current_device_info(&di);
+  if (st) return st;
+  const Tuning& tu = tuning();
+  static const int32_t kLens = 0;  // stands for a device seq_len array (batch > 1)
+  Call c{};
+  c.batch = batch;
+  c.n_heads = n_heads;
+  c.n_kv = n_kv_heads;
+  c.hd = head_dim;
+  c.single_len = (int32_t)seq;
+  c.seq_len = batch > 1 ? &kLens : nullptr;
+  c.who = who;
+  if (takes_short_path(c, tu)) {
+    const uint32_t C = nwd::decode_short_cluster(seq, tu.short_cta_rows);
+    *kernel = 1;
+    *grid = (int)(n_kv_heads * C);
+    *split = (int)C;
+    *cluster = C > 1 ? (int)C : 0;
+    *groups = 0;
+    return ok();
+  }
+  Plan pl;
+  st = plan_split(c, di, tu, &pl);
+  if (st) return st;
+  *kernel = 0;
+  *grid = (int)pl.grid;
+  *split = (int)pl.split_k;
+  *cluster = (int)pl.cluster;
+  *groups = (int)pl.ng;
+  return ok();
 }
 
 int nwd_noalloc_check(uint32_t* device_error, void* stream) {

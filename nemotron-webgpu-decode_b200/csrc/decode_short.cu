@@ -293,6 +293,16 @@ namespace nwd {
 
 uint32_t decode_short_max_rows() { return SHORT_ROWS; }
 
+uint32_t decode_short_cluster(uint32_t L, uint32_t cta_rows) {
+  if (cta_rows == 0 || cta_rows > CTA_ROWS) cta_rows = CTA_ROWS;
+  uint32_t C = 1;
+  if (L > CTA_ROWS) {
+    C = (L + cta_rows - 1) / cta_rows;
+    if (C > MAX_CLUSTER) C = MAX_CLUSTER;
+  }
+  return C;
+}
+
 int launch_decode_short(const uint16_t* q, const uint16_t* k_new, const uint16_t* v_new,
                         uint16_t* k_cache, uint16_t* v_cache, uint16_t* o, uint32_t L,
                         uint32_t n_kv, uint32_t group, float scale_log2, bool append,
@@ -300,15 +310,10 @@ int launch_decode_short(const uint16_t* q, const uint16_t* k_new, const uint16_t
   if (L == 0 || L > SHORT_ROWS || group > (uint32_t)SGMAX)
     return fail(NWD_ERR_UNSUPPORTED, "%s: short decode path needs 1..%u rows and group <= %d", who,
                 SHORT_ROWS, SGMAX);
-  if (cta_rows == 0 || cta_rows > CTA_ROWS) cta_rows = CTA_ROWS;
   // one CTA per kv head while its rows fit one CTA (a cluster launch and its
   // barriers cost more than they save there), else a cluster of C CTAs of
   // about cta_rows rows each (never more than CTA_ROWS)
-  uint32_t C = 1;
-  if (L > CTA_ROWS) {
-    C = (L + cta_rows - 1) / cta_rows;
-    if (C > MAX_CLUSTER) C = MAX_CLUSTER;
-  }
+  const uint32_t C = decode_short_cluster(L, cta_rows);
   if ((L + C - 1) / C > CTA_ROWS) return fail(NWD_ERR_UNSUPPORTED, "%s: %u rows", who, L);
   if ((uint64_t)n_kv * C > 0x7fffffffull) return fail(NWD_ERR_UNSUPPORTED, "%s: too many kv heads", who);
   DeviceInfo di;

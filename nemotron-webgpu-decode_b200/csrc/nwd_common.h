@@ -41,6 +41,8 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // most 8 query heads per kv head, head_dim 128.  With append, row L - 1 comes
 // from k_new / v_new and is written to the caches.
 uint32_t decode_short_max_rows();
+// CTAs per kv head the short kernel uses for L rows (1: no cluster).
+uint32_t decode_short_cluster(uint32_t L, uint32_t cta_rows);
 int launch_decode_short(const uint16_t* q, const uint16_t* k_new, const uint16_t* v_new,
                         uint16_t* k_cache, uint16_t* v_cache, uint16_t* o, uint32_t L,
                         uint32_t n_kv, uint32_t group, float scale_log2, bool append,

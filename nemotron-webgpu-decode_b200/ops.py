@@ -393,6 +393,17 @@ def prefetch_l2(buffers, stream=None) -> None:
          n, _stream(stream))
 
 
+def decode_plan(batch: int, n_heads: int, n_kv_heads: int, seq: int, head_dim: int = 128):
+    """How a decode call of this shape runs on the current device (no launch):
+    {kernel: "split"|"short", grid, split, cluster, groups} (nwd_attn_decode_plan)."""
+    v = [ctypes.c_int() for _ in range(5)]
+    call("nwd_attn_decode_plan", batch, n_heads, n_kv_heads, head_dim, seq,
+         *[ctypes.byref(x) for x in v])
+    k, grid, split, cluster, groups = (int(x.value) for x in v)
+    return {"kernel": "short" if k == 1 else "split", "grid": grid, "split": split,
+            "cluster": cluster, "groups": groups}
+
+
 def fill_normal(t: torch.Tensor, seed: int, offset: int = 0, stream=None) -> torch.Tensor:
     """Fill an fp16 tensor with the deterministic N(0,1) stream (bit-identical to the CPU
     generator used by the tests)."""
