@@ -2,23 +2,30 @@
 """Decode-attention bench: tokens/s and achieved HBM bandwidth on B200.
 
 Default workload (the config the metric's 1/2/4/8-GPU
-scaling is quoted on): 256 independent sequences per GPU, Hq=32, Hkv=8,
-d=128, per-sequence KV lengths drawn uniformly from [512, 8192] (seed 3),
-stored contiguously per sequence in one pool, fp16 q/K/V from the
-deterministic N(0,1) generator.  One step = the engine's attention-layer step
-for every sequence: append one K/V row at its position and attend over all of
-its rows (one fused launch of the library's decode kernel).  Positions cycle
-over 16 rows so every step attends L_b+1 .. L_b+16 rows (the workload stays at
-config 3's lengths however many steps run).  Sequences shard across GPUs with
-no communication; each GPU runs its own 256-sequence batch (weak scaling).
+scaling is quoted on): 256 independent sequences, Hq=32, Hkv=8, d=128,
+per-sequence KV lengths drawn uniformly from [512, 8192] (seed 3), stored
+contiguously per sequence in one pool, fp16 q/K/V from the deterministic
+N(0,1) generator.  One step = the engine's attention-layer step for every
+sequence: append one K/V row at its position and attend over all of its rows
+(one fused launch of the library's decode kernel).  Positions cycle over 16
+rows so every step attends L_b+1 .. L_b+16 rows (the workload stays at config
+3's lengths however many steps run).  On N GPUs the 256 sequences are split
+across the GPUs, balanced by rows, with no communication (strong scaling;
+``--scaling weak`` runs 256 sequences on every GPU instead).
+
+The same line carries two sub-objects (skipped with ``--no-extras``):
+``config5``, the long-context step (4 sequences x 1 048 576 rows, each
+sequence's rows sharded over the N GPUs, NCCL all-gather of the partials and
+the merge inside the library), with the exchange's measured share of the step;
+and ``config2``, the single-sequence length sweep on rank 0.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl nwd|reference]
-                  [--config 3|1|2|4|5|6] [--scaling weak|strong]
+                  [--config 3|1|2|4|5|6] [--scaling strong|weak] [--no-extras]
 
-Other configs: 1 engine trace and 2 length sweep (single sequence, CUDA-graph
-replay), 4 chunked causal prefill (tcgen05), 5 long-context split-KV sharded
-over the GPUs (NCCL all-gather + merge), 6 the model's 4 attention layers with
-their q4 projections (q/k/v + append, attention, o_proj + residual).
+Other configs as lines of their own: 1 engine trace and 2 length sweep (single
+sequence, CUDA-graph replay), 4 chunked causal prefill (tcgen05), 5 the
+long-context step, 6 the model's 4 attention layers with their q4 projections
+(q/k/v + append, attention, o_proj + residual).
 
 ``--impl reference`` times the reference's algorithm on the host CPU: the
 reference is WGSL for a browser WebGPU device, which this machine cannot run,
@@ -183,13 +190,26 @@ def config3_lengths():
     return np.random.default_rng(3).integers(512, 8193, 256).astype(np.int64)
 
 
+def strong_assignment(L, world):
+    """Sequence indices of each rank for a strong split, balanced by rows: the
+    longest sequence first, each to the rank holding the fewest rows so far
+    (ties to the lower rank).  The step time is the slowest rank's, so rows,
+    not sequence counts, are what must be even."""
+    sums = [0] * world
+    sets = [[] for _ in range(world)]
+    for i in np.argsort(-np.asarray(L), kind="stable"):
+        r = min(range(world), key=lambda x: (sums[x], x))
+        sets[r].append(int(i))
+        sums[r] += int(L[i])
+    return [sorted(s) for s in sets]
+
+
 def rank_lengths(rank, world, scaling, batch=None):
     L = config3_lengths()
     if batch:
         L = L[:batch]  # profiling captures: the first `batch` sequences
-    if scaling == "strong":
-        per = len(L) // world
-        return L[rank * per:(rank + 1) * per]
+    if scaling == "strong" and world > 1:
+        return L[strong_assignment(L, world)[rank]]
     return L
 
 
@@ -204,6 +224,15 @@ def max_over_ranks(values, dist=None, device=None):
     t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
     if dist is not None and dist.is_initialized() and dist.get_world_size() > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t.tolist()]
+
+
+def sum_over_ranks(values, dist=None, device=None):
+    """Element-wise sum of per-rank numbers (work counts) across ranks (no-op at N=1)."""
+    import torch
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
+    if dist is not None and dist.is_initialized() and dist.get_world_size() > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
     return [float(x) for x in t.tolist()]
 
 
@@ -323,7 +352,7 @@ def run_reference(args):
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "impl": "reference",
         "config": {"workload": "config3-batched-ragged-decode (sample)", "heads": HQ,
                    "kv_heads": HKV, "head_dim": HD, "sample_sequences": nseq,
@@ -342,6 +371,86 @@ def run_reference(args):
 
 # ------------------------------------------------------------------ GPU arm
 
+def e2e_config3(W, torch, dev, args, s, barrier):
+    """Config 3 end to end through ops.kv_append_attention_batched (ctypes -> C ABI)
+    with host buffers: per step, q / k_new / v_new / pos from pinned host memory
+    (H2D) and o back to pinned host memory (D2H), read by the host.  Two buffer
+    sets: step x's inputs cross on one copy stream while step x-1 computes, step
+    x's o crosses on another while step x+1 computes; the host waits for step
+    x-1's output event before issuing step x+1.  Device-timed from the first
+    copy to the last output landing (events on the compute stream, which waits
+    for both copy streams at the end)."""
+    comp = torch.cuda.current_stream()
+    cin, cout = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    pin = dict(pin_memory=True)
+    q_h = W.q.cpu().pin_memory()
+    kn_h = W.kn.cpu().pin_memory()
+    vn_h = W.vn.cpu().pin_memory()
+    pos_h = torch.tensor(W.pos_host).pin_memory()  # [cycle, B]
+    o_h = [torch.empty(W.B, HQ, HD, dtype=torch.float16, **pin) for _ in range(2)]
+    q_d = [torch.empty_like(W.q) for _ in range(2)]
+    kn_d = [torch.empty_like(W.kn) for _ in range(2)]
+    vn_d = [torch.empty_like(W.vn) for _ in range(2)]
+    pos_d = [torch.empty(W.B, dtype=torch.int32, device=dev) for _ in range(2)]
+    o_d = [torch.empty_like(W.o) for _ in range(2)]
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    in_ready = [ev(), ev()]
+    done = [ev(), ev()]
+    out_done = [ev(), ev()]
+    used = [False, False]
+    reads = []
+
+    def step(x):
+        i = x & 1
+        with torch.cuda.stream(cin):
+            if used[i]:
+                cin.wait_event(done[i])  # buffer set i's previous step has read its inputs
+            q_d[i].copy_(q_h, non_blocking=True)
+            kn_d[i].copy_(kn_h, non_blocking=True)
+            vn_d[i].copy_(vn_h, non_blocking=True)
+            pos_d[i].copy_(pos_h[x % POS_CYCLE], non_blocking=True)
+            in_ready[i].record(cin)
+        comp.wait_event(in_ready[i])
+        if used[i]:
+            comp.wait_event(out_done[i])  # o_d[i] has been copied out
+        W.step(x, q=q_d[i], kn=kn_d[i], vn=vn_d[i], pos=pos_d[i], o=o_d[i])
+        done[i].record(comp)
+        with torch.cuda.stream(cout):
+            cout.wait_event(done[i])
+            o_h[i].copy_(o_d[i], non_blocking=True)
+            out_done[i].record(cout)
+        used[i] = True
+        # the host reads step x-1's result before it issues step x+1
+        j = i ^ 1
+        if prev[0] is not None:
+            out_done[j].synchronize()
+            reads.append(float(o_h[j][0, 0, 0]))
+        prev[0] = x
+
+    prev = [None]
+    for _ in range(args.warmup):
+        step(s)
+        s += 1
+    comp.wait_stream(cout)
+    barrier()
+    prev[0] = None
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(comp)
+    cin.wait_stream(comp)
+    for _ in range(args.steps):
+        step(s)
+        s += 1
+    comp.wait_stream(cout)
+    end.record(comp)
+    end.synchronize()
+    reads.append(float(o_h[(s - 1) & 1][0, 0, 0]))  # the last step's result
+    barrier()
+    h2d = W.B * (HQ * HD * 2 + 2 * HKV * HD * 2 + 4)
+    d2h = W.B * HQ * HD * 2
+    return {"ms": start.elapsed_time(end), "h2d": h2d, "d2h": d2h, "s": s,
+            "finite": all(np.isfinite(reads))}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -350,7 +459,11 @@ def main():
     ap.add_argument("--impl", choices=["nwd", "reference"], default="nwd")
     ap.add_argument("--config", choices=["3", "1", "2", "4", "5", "6"], default="3",
                     help="BASELINE config (6 = the attention layers with their q4 projections)")
-    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="strong",
+                    help="config 3 at N>1: strong (the 256 sequences split across the GPUs, "
+                         "balanced by rows) or weak (256 sequences on every GPU)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="config 3: skip the config-5 and config-2 sub-objects of the line")
     ap.add_argument("--ramp-seconds", type=float, default=1.0)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -444,75 +557,73 @@ def main():
     kern_ms = statistics.mean(launch_ms)
     kern_gbs = statistics.mean(rb) / (kern_ms * 1e-3) / 1e9
 
-    # e2e: host buffers through the public API, H2D inputs + D2H output every step
+    # e2e: host buffers through the public API, every step's inputs copied in from
+    # pinned host memory and its output copied back and read by the host, all
+    # inside the timed region.  Double-buffered: step x's inputs cross on a copy
+    # stream while step x-1 computes, its output crosses on a second copy stream,
+    # and the host waits for step x-1's output (not for the whole stream).
     e2e = None
     if not args.no_e2e:
-        pin = dict(pin_memory=True)
-        q_h = W.q.cpu().pin_memory()
-        kn_h = W.kn.cpu().pin_memory()
-        vn_h = W.vn.cpu().pin_memory()
-        pos_h = torch.tensor(W.pos_host).pin_memory()
-        o_h = torch.empty(W.B, HQ, HD, dtype=torch.float16, **pin)
-        q_d, kn_d, vn_d = torch.empty_like(W.q), torch.empty_like(W.kn), torch.empty_like(W.vn)
-        pos_d = torch.empty(W.B, dtype=torch.int32, device=dev)
-        o_d = torch.empty_like(W.o)
-        stream = torch.cuda.current_stream()
-
-        def e2e_step(x):
-            q_d.copy_(q_h, non_blocking=True)
-            kn_d.copy_(kn_h, non_blocking=True)
-            vn_d.copy_(vn_h, non_blocking=True)
-            pos_d.copy_(pos_h[x % POS_CYCLE], non_blocking=True)
-            W.step(x, q=q_d, kn=kn_d, vn=vn_d, pos=pos_d, o=o_d)
-            o_h.copy_(o_d, non_blocking=True)
-            stream.synchronize()
-            return float(o_h[0, 0, 0])  # the host reads the step's result
-
-        for _ in range(args.warmup):
-            e2e_step(s)
-            s += 1
-        barrier()
-        es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        es.record()
-        for _ in range(args.steps):
-            e2e_step(s)
-            s += 1
-        ee.record()
-        ee.synchronize()
-        barrier()
-        e2e_ms = es.elapsed_time(ee)
-        h2d = W.B * (HQ * HD * 2 + 2 * HKV * HD * 2 + 4)
-        d2h = W.B * HQ * HD * 2
-        e2e = {"ms": e2e_ms, "h2d": h2d, "d2h": d2h}
+        e2e = e2e_config3(W, torch, dev, args, s, barrier)
+        s = e2e.pop("s")
 
     err = W.ws.check()
     if err:
         print(f"device error word {err} after the bench", file=sys.stderr)
         return 3
+    if e2e and not e2e["finite"]:
+        print("non-finite output read back in the e2e pass", file=sys.stderr)
+        return 3
 
-    # max over ranks
+    # max over ranks (times), sums over ranks (work)
     ms_max, e2e_ms_max = max_over_ranks([ms, e2e["ms"] if e2e else 0.0], dist, dev)
+    n_seq, bytes_timed, h2d, d2h = sum_over_ranks(
+        [W.B, sum(step_bytes_timed), e2e["h2d"] if e2e else 0, e2e["d2h"] if e2e else 0],
+        dist, dev)
+    clocks = None
     if sampler:
         sampler.stop()
+        clocks = sampler.summary(t0, t1)
+    cpu_L, cpu_seeds = W.L, W.seeds
+    del W
+    torch.cuda.empty_cache()
+
+    # the long-context sharded step and the single-sequence sweep, recorded in
+    # the same line (every rank takes part in the sharded step)
+    extra5 = extra2 = None
+    if not args.no_extras:
+        # an error here is recorded in the sub-object and costs the headline
+        # nothing (every wait inside is bounded: the communicator's deadlines,
+        # the process group's timeout)
+        try:
+            extra5 = measure_config5(args, ops, torch, dist, dev, rank, world, sub=True)
+        except Exception as e:  # noqa: BLE001
+            extra5 = {"workload": "config5-long-context-split-kv", "error": str(e)[:300]}
+        if rank == 0:
+            try:
+                extra2 = [summarise_small(x) for x in small_config_lines(args, ops, torch, dev, "2")]
+            except Exception as e:  # noqa: BLE001
+                extra2 = [{"workload": "config2", "error": str(e)[:300]}]
     if rank == 0:
-        tokens = W.B * world * args.steps
+        tokens = n_seq * args.steps
         value = tokens / (ms_max * 1e-3)
-        total_bytes = sum(step_bytes_timed) * world
         peak, peak_kind = peaks()
-        clocks = sampler.summary(t0, t1) if sampler else None
         traffic = profiled_traffic("decode_kernel_config3_traffic")
+        strong = args.scaling == "strong" or world == 1
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
-            "higher_is_better": True, "scaling": "weak" if args.scaling == "weak" else "strong",
+            "higher_is_better": True, "scaling": "strong" if strong else "weak",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "hbm_tbs": total_bytes / (ms_max * 1e-3) / 1e12,
+            "hbm_tbs": bytes_timed / (ms_max * 1e-3) / 1e12,
             "config": {
-                "workload": "config3-batched-ragged-decode", "sequences_per_gpu": W.B,
-                "global_batch": W.B * world, "heads": HQ, "kv_heads": HKV, "head_dim": HD,
+                "workload": "config3-batched-ragged-decode", "global_batch": int(n_seq),
+                "sequences_per_gpu": (f"{int(n_seq)} split across {world} GPUs, balanced by rows"
+                                      if strong and world > 1 else int(n_seq) // world),
+                "heads": HQ, "kv_heads": HKV, "head_dim": HD,
                 "kv_len": "U[512,8192] seed 3 (+1..16 cycling append rows)",
                 "accumulate": "f32", "step": "fused kv_append + decode attention, 1 launch",
-                "l2": "inputs larger than L2 (~4.6 GB of K/V per step per GPU)",
+                "l2": "inputs larger than L2 (~4.6 GB of K/V per step in total)",
                 "parallelism": f"sequence-sharded x{world}, no communication"},
             "roofline": {"bound": "hbm", "achieved": kern_gbs, "peak": peak, "unit": "GB/s",
                          "frac": kern_gbs / peak, "traffic": traffic,
@@ -523,15 +634,21 @@ def main():
             "clocks": clocks,
         }
         if e2e:
-            line["e2e"] = {"value": W.B * world * args.steps / (e2e_ms_max * 1e-3),
-                           "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"] * world,
-                           "d2h_bytes_per_step": e2e["d2h"] * world,
+            line["e2e"] = {"value": tokens / (e2e_ms_max * 1e-3),
+                           "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
+                           "d2h_bytes_per_step": int(d2h),
                            "ms_per_step": e2e_ms_max / args.steps,
                            "path": "ops.kv_append_attention_batched (ctypes -> libnwd.so C ABI), "
-                                   "pinned host buffers, per-step stream sync"}
+                                   "pinned host buffers; inputs cross on a copy stream while the "
+                                   "previous step computes, o crosses on a second copy stream, "
+                                   "the host reads step x-1's o before issuing step x+1"}
+        if extra5:
+            line["config5"] = extra5
+        if extra2:
+            line["config2"] = extra2
         if world == 1 and not args.no_cpu_baseline:
             oracle = import_oracle()
-            line["cpu_baseline"] = cpu_baseline(oracle, W.L, W.seeds, seconds=args.cpu_seconds)
+            line["cpu_baseline"] = cpu_baseline(oracle, cpu_L, cpu_seeds, seconds=args.cpu_seconds)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -539,15 +656,40 @@ def main():
     return 0
 
 
+def summarise_small(ln):
+    """The figures of a config-2 line kept in the headline line's sub-object."""
+    return {"workload": ln["config"]["workload"], "kv_len": ln["config"]["kv_len"],
+            "heads": ln["config"]["heads"], "ms_per_step": ln["ms_per_step"],
+            "tokens_per_s": ln["value"], "achieved_gbs": ln["roofline"]["achieved"],
+            "frac": ln["roofline"]["frac"], "steps": ln["steps"], "l2": ln["config"]["l2"]}
+
+
 def run_small_configs(args, ops, torch, dev, rank, world):
-    """Secondary lines: config 1 (engine trace) and config 2 (L sweep), Hq=40 (engine/config.js).
+    """Secondary lines: config 1 (engine trace) and config 2 (L sweep), Hq=40
+    (engine/config.js), on rank 0 (a single sequence does not shard: replicas only)."""
+    if rank != 0:
+        return 0
+    sampler = start_clocks(torch, dev, rank)
+    t0 = time.monotonic()
+    out = small_config_lines(args, ops, torch, dev, args.config)
+    t1 = time.monotonic()
+    if sampler:
+        sampler.stop()
+        clocks = sampler.summary(t0, t1)
+        for ln in out:
+            ln["clocks"] = clocks
+    for ln in out:
+        print(json.dumps(ln), flush=True)
+    return 0
+
+
+def small_config_lines(args, ops, torch, dev, which):
+    """Lines of config 1 (which="1") or the config-2 sweep (which="2").
 
     These single-sequence steps take microseconds, so the steps are captured
     once in a CUDA graph (one fused launch per step, in order) and the graph is
     replayed: the timing is the GPU's, not Python's launch overhead.
     """
-    if rank != 0:
-        return 0
     engine = importlib.import_module(PKG + ".engine")
     peak, _ = peaks()
     nh = 40
@@ -639,9 +781,7 @@ def run_small_configs(args, ops, torch, dev, rank, world):
                 "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
                              "frac": gbs / peak}}
 
-    sampler = start_clocks(torch, dev, rank)
-    t0 = time.monotonic()
-    if args.config == "1":
+    if which == "1":
         layer = engine.DecodeAttention(nh, HKV, HD, 256)
         ops.fill_normal(layer.k_cache, 11)
         ops.fill_normal(layer.v_cache, 12)
@@ -671,15 +811,7 @@ def run_small_configs(args, ops, torch, dev, rank, world):
                             {"kv_len": L, "l2": f"{copies} sequences visited in turn "
                              f"({copies * L * 4096 >> 20} MB of K/V > L2); no flush"}))
             del layers
-    t1 = time.monotonic()
-    if sampler:
-        sampler.stop()
-        clocks = sampler.summary(t0, t1)
-        for ln in out:
-            ln["clocks"] = clocks
-    for ln in out:
-        print(json.dumps(ln), flush=True)
-    return 0
+    return out
 
 
 def run_config4(args, ops, torch, dist, dev, rank, world):
@@ -1027,14 +1159,28 @@ def cpu_baseline_config6(args):
 
 
 def run_config5(args, ops, torch, dist, dev, rank, world):
+    """--config 5: the long-context sharded step as its own line."""
+    line = measure_config5(args, ops, torch, dist, dev, rank, world, sub=False)
+    err = line.get("device_error", 0) if line else 0
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0 if err == 0 else 3
+
+
+def measure_config5(args, ops, torch, dist, dev, rank, world, sub=False):
     """4 sequences x 1 048 576 rows (Hq=32, Hkv=8), each sequence's
-    rows sharded contiguously over the ranks; a step is the shard partial on every
-    GPU, one NCCL all-gather of the partials and the LSE merge (mgpu.ShardedDecode).
-    The K/V data is the same stream whatever the rank count (fill offsets follow
-    the global row index), so every N computes the same O."""
+    rows sharded contiguously over the ranks (strong scaling); a step is the shard
+    partial on every GPU, one NCCL all-gather of the packed partials and the LSE
+    merge, run by the library (nwd_mgpu_decode_step) at N > 1, and the partial +
+    merge at N = 1.  The K/V data is the same stream whatever the rank count (fill
+    offsets follow the global row index), so every N computes the same O.  Returns
+    the line (rank 0) or None; with sub=True the figures the config-3 line keeps."""
     mgpu = importlib.import_module(PKG + ".mgpu")
     B, L = 4, 1 << 20
-    if args.kv_len:
+    if args.kv_len and not sub:
         L = args.kv_len
     sd = mgpu.ShardedDecode([L] * B, HQ, HKV, HD, device=dev)
     row_elems = HKV * HD
@@ -1047,30 +1193,56 @@ def run_config5(args, ops, torch, dist, dev, rank, world):
     q = ops.fill_normal(torch.empty(B, HQ, HD, dtype=torch.float16, device=dev), 5002)
     o = torch.empty(B, HQ, HD, dtype=torch.float16, device=dev)
     torch.cuda.synchronize()
+    steps = args.steps
+    warmup = args.warmup
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
-    sampler = start_clocks(torch, dev, rank)
-    for _ in range(args.warmup):
+    sampler = None if sub else start_clocks(torch, dev, rank)
+    for _ in range(warmup):
         sd.step(q, o)
+    sd.sync()
     barrier()
     t0 = time.monotonic()
     a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         sd.step(q, o)
     e.record()
+    sd.sync()  # bounded by the communicator's deadline at N > 1
     e.synchronize()
     barrier()
     t1 = time.monotonic()
     if sampler:
         sampler.stop()
     ms = a.elapsed_time(e)
+    # where a step's time goes: the shard partial, and the all-gather + merge
+    R = min(steps, 20)
+    part_ms, xchg_ms = [], []
+    if sd.comm is not None:
+        sd.comm.set_timing(True)
+        for _ in range(R):
+            sd.step(q, o)
+            sd.sync()
+            pm, xm = sd.comm.step_times()
+            part_ms.append(pm)
+            xchg_ms.append(xm)
+        sd.comm.set_timing(False)
+    else:
+        for _ in range(R):
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record()
+            sd.partial_fn(q)
+            e1.record()
+            ops.merge_packed(sd.packed.unsqueeze(0), o)
+            e2.record()
+            e2.synchronize()
+            part_ms.append(e0.elapsed_time(e1))
+            xchg_ms.append(e1.elapsed_time(e2))
     # roofline of the shard kernel alone (per-launch events, same stream)
-    R = min(args.steps, 20)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(R)]
     for i in range(R):
@@ -1086,58 +1258,76 @@ def run_config5(args, ops, torch, dist, dev, rank, world):
     q_h = q.cpu().pin_memory()
     o_h = torch.empty(B, HQ, HD, dtype=torch.float16, pin_memory=True)
     stream = torch.cuda.current_stream()
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         q.copy_(q_h, non_blocking=True)
         sd.step(q, o)
         o_h.copy_(o, non_blocking=True)
+        sd.sync()
         stream.synchronize()
     barrier()
     a2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a2.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         q.copy_(q_h, non_blocking=True)
         sd.step(q, o)
         o_h.copy_(o, non_blocking=True)
+        sd.sync()
         stream.synchronize()
     e2.record()
     e2.synchronize()
     barrier()
     e2e_ms = a2.elapsed_time(e2)
-    ms_max, e2e_max = max_over_ranks([ms, e2e_ms], dist, dev)
+    ms_max, e2e_max, _, part_max, xchg_max = max_over_ranks(
+        [ms, e2e_ms, kern_ms, statistics.mean(part_ms), statistics.mean(xchg_ms)], dist, dev)
     err = sd.workspace.check()
-    if rank == 0:
-        peak, kind = peaks()
-        total_bytes = 4096.0 * B * L + B * HQ * HD * 4
-        line = {
-            "metric": METRIC, "value": B * args.steps / (ms_max * 1e-3), "unit": "tokens/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "hbm_tbs": total_bytes / (ms_max * 1e-3 / args.steps) / 1e12,
-            "config": {"workload": "config5-long-context-split-kv", "sequences": B,
-                       "kv_len": L, "heads": HQ, "kv_heads": HKV, "head_dim": HD,
-                       "parallelism": f"rows sharded x{world}, NCCL all-gather of partials",
-                       "step": "shard partial + all-gather + LSE merge"},
-            "roofline": {"bound": "hbm", "achieved": kern_bytes / (kern_ms * 1e-3) / 1e9,
-                         "peak": peak, "unit": "GB/s",
-                         "frac": kern_bytes / (kern_ms * 1e-3) / 1e9 / peak,
-                         "kernel": "decode_kernel (partial mode), per rank",
-                         "launch_ms": kern_ms, "peak_source": kind,
-                         # committed ncu figure for the whole 1-GPU launch (4 x 2^20 rows),
-                         # scaled to this rank's rows (traffic is proportional to rows)
-                         "traffic": (None if traffic5 is None else
-                                     traffic5 * local_rows / (4.0 * (1 << 20)))},
-            "e2e": {"value": B * args.steps / (e2e_max * 1e-3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": B * HQ * HD * 2, "d2h_bytes_per_step": B * HQ * HD * 2},
-            "gpu_launches": 2 * args.steps,
-            "device_error": err,
-            "clocks": sampler.summary(t0, t1) if sampler else None,
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0 if err == 0 else 3
+    sd.close()
+    del sd
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    peak, kind = peaks()
+    total_bytes = 4096.0 * B * L + B * HQ * HD * 4
+    achieved = kern_bytes / (kern_ms * 1e-3) / 1e9
+    roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "kernel": "decode_kernel (partial mode), per rank",
+            "launch_ms": kern_ms, "peak_source": kind,
+            # committed ncu figure for the whole 1-GPU launch (4 x 2^20 rows),
+            # scaled to this rank's rows (traffic is proportional to rows)
+            "traffic": (None if traffic5 is None else
+                        traffic5 * local_rows / (4.0 * (1 << 20)))}
+    split = {"partial_ms": part_max, "exchange_ms": xchg_max,
+             "exchange_share": xchg_max / (part_max + xchg_max),
+             "how": ("CUDA events around the shard partial and around the NCCL all-gather + "
+                     "merge (nwd_mgpu_step_times), one synchronised step at a time, mean of "
+                     f"{R}, max over ranks" if world > 1 else
+                     f"CUDA events around the partial and the merge, mean of {R}")}
+    value = B * steps / (ms_max * 1e-3)
+    if sub:
+        return {"workload": "config5-long-context-split-kv", "sequences": B, "kv_len": L,
+                "scaling": "strong", "n_gpus": world, "value": value, "unit": "tokens/s",
+                "ms_per_step": ms_max / steps, "hbm_tbs": total_bytes / (ms_max * 1e-3 / steps)
+                / 1e12, "roofline": roof, "step_split": split, "device_error": err,
+                "e2e": {"value": B * steps / (e2e_max * 1e-3), "unit": "tokens/s",
+                        "h2d_bytes_per_step": B * HQ * HD * 2,
+                        "d2h_bytes_per_step": B * HQ * HD * 2}}
+    return {
+        "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": steps, "warmup": warmup,
+        "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "hbm_tbs": total_bytes / (ms_max * 1e-3 / steps) / 1e12,
+        "config": {"workload": "config5-long-context-split-kv", "sequences": B,
+                   "kv_len": L, "heads": HQ, "kv_heads": HKV, "head_dim": HD,
+                   "parallelism": f"rows sharded x{world}, NCCL all-gather of partials "
+                                  "(nwd_mgpu_decode_step)",
+                   "step": "shard partial + all-gather + LSE merge"},
+        "roofline": roof, "step_split": split,
+        "e2e": {"value": B * steps / (e2e_max * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": B * HQ * HD * 2, "d2h_bytes_per_step": B * HQ * HD * 2},
+        "gpu_launches": (3 if world > 1 else 2) * steps,
+        "device_error": err,
+        "clocks": sampler.summary(t0, t1) if sampler else None,
+    }
 
 
 if __name__ == "__main__":

@@ -97,3 +97,17 @@ def test_reference_arm_line(tmp_path):
     env["RANK"] = "1"
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=600, cwd=REPO)
     assert r.returncode == 0 and not [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_strong_split_is_balanced_by_rows(bench, world):
+    """Config 3 at N GPUs: every sequence on exactly one rank, and the ranks' row
+    totals (which set the step time, the slowest rank's) within one sequence of each
+    other; contiguous blocks of the seed-3 lengths are not."""
+    L = bench.config3_lengths()
+    sets = bench.strong_assignment(L, world)
+    assert sorted(i for s in sets for i in s) == list(range(len(L)))
+    sums = [int(L[s].sum()) for s in sets]
+    assert max(sums) - min(sums) <= 512, sums  # the shortest sequence bounds the gap
+    for r in range(world):
+        assert list(bench.rank_lengths(r, world, "strong")) == [int(L[i]) for i in sets[r]]

@@ -47,10 +47,12 @@ def test_bench_rank_helpers(tmp_path):
     for r in res:
         assert r["vals"] == [2.0, 10.0]  # max over ranks, element-wise
         assert r["weak_n"] == 256         # weak scaling: each GPU runs a full batch
-    assert len(res[0]["strong"]) == len(res[1]["strong"]) == 128
     assert res[0]["seeds"] != res[1]["seeds"]
+    # strong scaling: the 256 sequences split between the ranks, balanced by rows
     L = np.random.default_rng(3).integers(512, 8193, 256)
-    assert res[0]["strong"] + res[1]["strong"] == [int(x) for x in L]
+    assert sorted(res[0]["strong"] + res[1]["strong"]) == sorted(int(x) for x in L)
+    s0, s1 = sum(res[0]["strong"]), sum(res[1]["strong"])
+    assert abs(s0 - s1) <= 8192, (s0, s1)
 
 
 def test_missing_rank_ends_the_step_with_an_error(tmp_path):
