@@ -329,10 +329,20 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
     rows_local += L;
     max_local = max(max_local, L);
   }
-  if (rows_local)
-    atomicAdd(reinterpret_cast<unsigned long long*>(&misc->total_rows),
-              (unsigned long long)rows_local);
-  if (max_local) atomicMax(&misc->max_rows, max_local);
+  {
+    // reduce within the warp first: one shared-memory atomic per warp (every
+    // thread's atomics on the same two words serialised to 13 us at 256
+    // sequences)
+    unsigned long long ws = rows_local;
+    uint32_t wm = max_local;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      ws += __shfl_xor_sync(0xffffffffu, ws, o);
+      wm = max(wm, __shfl_xor_sync(0xffffffffu, wm, o));
+    }
+    if (lane == 0 && ws) atomicAdd(reinterpret_cast<unsigned long long*>(&misc->total_rows), ws);
+    if (lane == 0 && wm) atomicMax(&misc->max_rows, wm);
+  }
   uint32_t total32;
   uint32_t run = block_scan<NTHR>((uint32_t)rows_local, misc, &total32);  // syncs: sums final
   if (misc->total_rows >= (1ull << 32)) {
