@@ -251,6 +251,12 @@ int nwd_attn_merge_packed(const float* packed, uint16_t* o, uint32_t shards, uin
  * single-sequence attention (kernels/sparse_attn.wgsl:32-113, dispatched at
  * engine/runtime.js:391) to rows held by several GPUs.
  *
+ * When every rank can map every other rank's memory (NVLink / NVSwitch) the
+ * exchange runs over peer memory: the shard partial kernel writes each pair's
+ * partial into every rank's exchange buffer (allocated by the library with the
+ * driver's virtual-memory API, its file descriptor passed to the peers over a
+ * Unix-domain socket) and a merge kernel on each rank waits, bounded, for all
+ * ranks' flags; otherwise (or with NWD_MGPU_P2P=0) by NCCL all-gather.
  * NCCL is loaded at run time on the first nwd_mgpu_* call (NWD_NCCL_LIBRARY,
  * else libnccl.so.2 as the process finds it).  Communicators are
  * non-blocking: every wait (set-up, enqueue, step completion, finalize) runs
@@ -308,6 +314,13 @@ int nwd_mgpu_destroy(nwd_mgpu* m);
 int nwd_mgpu_abort(nwd_mgpu* m);
 /* The loaded NCCL's version code (e.g. 22809). */
 int nwd_mgpu_nccl_version(int* version);
+/* How the steps exchange partials: 1 = over peer memory (the partial kernel
+ * writes each pair's partial into every rank's exchange buffer, a merge
+ * kernel waits for all ranks' flags), -1 = NCCL all-gather + merge (some rank
+ * could not map every other rank's memory, or NWD_MGPU_P2P=0), 0 = not
+ * decided yet (no step made).  Decided collectively on the first step of a
+ * shape. */
+int nwd_mgpu_exchange_mode(nwd_mgpu* m, int* mode);
 
 /* ------------------------------------------------------------------ */
 /* Device memory and streams for hosts without a CUDA runtime          */

@@ -96,6 +96,7 @@ SIGNATURES = {
     "nwd_mgpu_destroy": (ctypes.c_int, [_P]),
     "nwd_mgpu_abort": (ctypes.c_int, [_P]),
     "nwd_mgpu_nccl_version": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "nwd_mgpu_exchange_mode": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_int)]),
     "nwd_set_device": (ctypes.c_int, [ctypes.c_int]),
     "nwd_device_count": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "nwd_alloc": (ctypes.c_int, [_sz, ctypes.POINTER(_P)]),

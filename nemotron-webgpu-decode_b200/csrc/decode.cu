@@ -95,6 +95,7 @@ struct Params {
   uint32_t prefetch;   // single sequence: K/V tiles per CTA prefetched into L2 before the wait
   uint32_t cluster;    // > 0: launched as clusters of this many CTAs, one cluster per kv
                        // head (split_k == cluster); the pieces merge over DSMEM
+  nwd::XchgDesc x;     // partial mode, x.world > 0: push each pair's partial to every rank
 };
 
 // ---- shared memory layout (offsets from a 1024-aligned base) ----
@@ -174,6 +175,24 @@ __device__ __forceinline__ bool consumer_sync(uint32_t bar, uint32_t& ph, volati
   const bool ok = warp_wait(bar, ph, abort, dev_err);
   ph ^= 1u;
   return ok;
+}
+
+// This step's exchange row `row` of the source rank (this rank) in
+// destination rank r's buffer.
+__device__ __forceinline__ float* xchg_row(const nwd::XchgDesc& x, uint32_t r, uint32_t row) {
+  const uint32_t par = x.epoch & 1u;
+  return x.data[r] + ((size_t)(par * x.world + x.rank) * x.R + row) * nwd::XCH_ROW;
+}
+// Marks pair `pair` of this rank as written on every rank: a system-scope
+// fence orders the partial's stores (made by this CTA's threads before a
+// barrier) before the flag stores, which release at system scope.
+__device__ __forceinline__ void xchg_publish(const nwd::XchgDesc& x, uint32_t pair) {
+  const uint32_t par = x.epoch & 1u;
+  __threadfence_system();
+  for (uint32_t r = 0; r < x.world; r++) {
+    uint32_t* f = x.flags[r] + (size_t)(par * x.world + x.rank) * x.P + pair;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(x.epoch) : "memory");
+  }
 }
 
 // Cluster-wide barrier over every thread of every CTA of the cluster (release
@@ -411,13 +430,25 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
     const size_t row0 = (size_t)b * p.n_heads;
     for (uint32_t i = tid; i < p.n_heads * (HD / 8); i += NTHR) {
       const size_t row = row0 + i / (HD / 8), d = (i % (HD / 8)) * 8;
-      if (p.partial) {
+      if (p.partial && p.x.world) {
+        for (uint32_t r = 0; r < p.x.world; r++) {
+          float* dst = xchg_row(p.x, r, (uint32_t)row);
+          *reinterpret_cast<float4*>(dst + d) = make_float4(0.f, 0.f, 0.f, 0.f);
+          *reinterpret_cast<float4*>(dst + d + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (d == 0) *reinterpret_cast<float2*>(dst + HD) = make_float2(-INFINITY, 0.f);
+        }
+      } else if (p.partial) {
         float4* dst = reinterpret_cast<float4*>(p.part_o + row * HD + d);
         dst[0] = dst[1] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (d == 0) *reinterpret_cast<float2*>(p.part_ml + row * 2) = make_float2(-INFINITY, 0.f);
       } else {
         *reinterpret_cast<uint4*>(p.o + row * HD + d) = make_uint4(0u, 0u, 0u, 0u);
       }
+    }
+    if (p.partial && p.x.world) {
+      __syncthreads();  // every thread's empty partials are written
+      if (tid == 0)
+        for (uint32_t hkv = 0; hkv < p.n_kv; hkv++) xchg_publish(p.x, b * p.n_kv + hkv);
     }
   }
 
@@ -928,7 +959,15 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
     }
     if (emit && g < G) {
       const size_t row = (size_t)b * p.n_heads + (size_t)hkv * G + g;
-      if (p.partial) {
+      if (p.partial && p.x.world) {
+        // the pair's partial straight into every rank's exchange slot
+        for (uint32_t r = 0; r < p.x.world; r++) {
+          float* dst = xchg_row(p.x, r, (uint32_t)row);
+          if (d0 == 0) *reinterpret_cast<float2*>(dst + HD) = make_float2(M, Ls);
+#pragma unroll
+          for (int j = 0; j < NV; j++) *reinterpret_cast<float4*>(dst + d0 + 4 * j) = o4[j];
+        }
+      } else if (p.partial) {
         if (d0 == 0) *reinterpret_cast<float2*>(p.part_ml + row * 2) = make_float2(M, Ls);
         float4* dst = reinterpret_cast<float4*>(p.part_o + row * HD + d0);
 #pragma unroll
@@ -943,6 +982,11 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
           *reinterpret_cast<uint2*>(p.o + row * HD + d0 + 4 * j) = v;
         }
       }
+    }
+    if (emit && p.partial && p.x.world) {
+      // every thread's stores of the pair's partial, then its flag on every rank
+      if (!consumer_sync(bar_csync, cph, abort_flag, &wsh->error)) break;
+      if (ct == 0) xchg_publish(p.x, b * p.n_kv + hkv);
     }
   }
   }  // consumer warps
@@ -1137,6 +1181,7 @@ struct Call {
   size_t ws_bytes;
   void* stream;
   const char* who;
+  const nwd::XchgDesc* x;  // partial mode only: push to the exchange buffers
 };
 
 int check_shape(uint32_t n_heads, uint32_t n_kv, uint32_t hd, const char* who) {
@@ -1243,7 +1288,7 @@ int launch(const Call& c) {
   int st = check_shape(c.n_heads, c.n_kv, c.hd, c.who);
   if (st) return st;
   if (!c.q || !c.k_pool || !c.v_pool || (!c.partial && !c.o) ||
-      (c.partial && (!c.part_o || !c.part_ml)) || (c.append && (!c.k_new || !c.v_new)))
+      (c.partial && !c.x && (!c.part_o || !c.part_ml)) || (c.append && (!c.k_new || !c.v_new)))
     return fail(NWD_ERR_INVALID, "%s: null pointer", c.who);
   if (!aligned16(c.q) || !aligned16(c.k_pool) || !aligned16(c.v_pool) ||
       (c.o && !aligned16(c.o)) || (c.part_o && !aligned16(c.part_o)) ||
@@ -1315,6 +1360,7 @@ int launch(const Call& c) {
   p.scale_log2 = scale * 1.4426950408889634f;
   p.append = c.append ? 1u : 0u;
   p.partial = c.partial ? 1u : 0u;
+  if (c.x) p.x = *c.x;  // memset above leaves world = 0 otherwise
   p.min_chunk = tu.min_chunk;
   p.prefetch = tu.prefetch;
   p.pair_max = tu.pair_max;
@@ -1391,6 +1437,30 @@ int noalloc_scratch(int device, void* stream, void** out) {
 }  // namespace
 
 using namespace nwd;
+
+namespace nwd {
+
+int decode_partial_xchg(const uint16_t* q, const uint16_t* k_pool, const uint16_t* v_pool,
+                        uint64_t pool_rows, const int64_t* row_offset, const int32_t* seq_len,
+                        uint32_t batch, uint32_t n_heads, uint32_t n_kv, uint32_t head_dim,
+                        float scale, void* workspace, size_t ws_bytes, void* stream,
+                        const XchgDesc& x) {
+  if (!row_offset || !seq_len) return fail(NWD_ERR_INVALID, "decode_partial_xchg: null pointer");
+  if (x.world == 0 || x.world > (uint32_t)XCH_MAX_RANKS || x.rank >= x.world || x.epoch == 0 ||
+      x.R != batch * n_heads || x.P != batch * n_kv)
+    return fail(NWD_ERR_INVALID, "decode_partial_xchg: exchange descriptor does not match");
+  for (uint32_t r = 0; r < x.world; r++)
+    if (!x.data[r] || !x.flags[r] || !aligned16(x.data[r]))
+      return fail(NWD_ERR_INVALID, "decode_partial_xchg: exchange buffer %u missing", r);
+  Call c{};
+  c.q = q; c.k_pool = k_pool; c.v_pool = v_pool; c.pool_rows = pool_rows;
+  c.row_offset = row_offset; c.seq_len = seq_len; c.batch = batch; c.n_heads = n_heads;
+  c.n_kv = n_kv; c.hd = head_dim; c.scale = scale; c.partial = true; c.ws = workspace;
+  c.ws_bytes = ws_bytes; c.stream = stream; c.who = "nwd_mgpu_decode_step"; c.x = &x;
+  return launch(c);
+}
+
+}  // namespace nwd
 
 extern "C" {
 

@@ -82,6 +82,37 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 }
 #endif
 
+// ---- the long-context exchange over peer memory (mgpu.cu, xchg.cu) ----
+// Every rank owns one exchange buffer in its own GPU memory, mapped by every
+// rank: [2 parities][world source ranks][R rows][XCH_ROW floats] of partials
+// (o[128], then m, l; R = batch * n_heads, row = b * n_heads + h), then
+// [2 parities][world][P pairs] u32 flags (P = batch * n_kv, pair = b * n_kv +
+// hkv).  Step `epoch` (from 1) uses parity epoch & 1: source rank r writes its
+// partials of a pair into every rank's slot [parity][r] and then, at system
+// scope with release, the pair's flag there to `epoch`; each rank's merge
+// waits until all world flags of a pair read `epoch`.
+constexpr int XCH_MAX_RANKS = 8;
+constexpr uint32_t XCH_ROW = 132;  // floats per (b, h) row: o[128], m, l, pad (16-byte rows)
+struct XchgDesc {
+  float* data[XCH_MAX_RANKS];      // destination rank r's buffer, as mapped in this process
+  uint32_t* flags[XCH_MAX_RANKS];  // destination rank r's flag block
+  uint32_t world, rank, epoch, R, P;
+};
+inline size_t xchg_data_floats(uint32_t world, uint32_t R) { return (size_t)2 * world * R * XCH_ROW; }
+inline size_t xchg_bytes(uint32_t world, uint32_t R, uint32_t P) {
+  return xchg_data_floats(world, R) * 4 + (size_t)2 * world * P * 4;
+}
+// The shard partial of every (sequence, kv head) pair pushed to every rank
+// (decode.cu), and the waiting merge of the pairs' partials into O (xchg.cu).
+int decode_partial_xchg(const uint16_t* q, const uint16_t* k_pool, const uint16_t* v_pool,
+                        uint64_t pool_rows, const int64_t* row_offset, const int32_t* seq_len,
+                        uint32_t batch, uint32_t n_heads, uint32_t n_kv, uint32_t head_dim,
+                        float scale, void* workspace, size_t ws_bytes, void* stream,
+                        const XchgDesc& x);
+int launch_xchg_merge(const float* own_data, const uint32_t* own_flags, uint16_t* o,
+                      uint32_t world, uint32_t epoch, uint32_t batch, uint32_t n_heads,
+                      uint32_t n_kv, uint32_t* dev_err, void* stream);
+
 // ---- workspace layout shared by the decode kernels ----
 // [0, 256)            header: error word, scheduler counters
 // [256, +tickets)     uint32 per (sequence, kv head) merge tickets

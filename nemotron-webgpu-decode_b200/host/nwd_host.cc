@@ -404,14 +404,16 @@ int run_mgpu(const Args& a) {
     printf("{\"ok\": false, \"failed\": \"writing --out\"}\n");
     return 2;
   }
-  int nccl_version = 0;
+  int nccl_version = 0, mode = 0;
   need(nwd_mgpu_nccl_version(&nccl_version), "nwd_mgpu_nccl_version");
+  need(nwd_mgpu_exchange_mode(comm, &mode), "nwd_mgpu_exchange_mode");
   need(nwd_mgpu_destroy(comm), "nwd_mgpu_destroy");
   for (void* p : {kp, vp, q, o, d_offs, d_lens, ws}) need(nwd_free(p), "nwd_free");
   need(nwd_stream_destroy(stream), "nwd_stream_destroy");
   printf("{\"ok\": %s, \"mode\": \"mgpu\", \"rank\": %d, \"world\": %d, \"steps\": %d, "
-         "\"device_error\": %u, \"nccl_version\": %d}\n",
-         dev_err == 0 ? "true" : "false", rank, world, done, dev_err, nccl_version);
+         "\"device_error\": %u, \"nccl_version\": %d, \"exchange\": \"%s\"}\n",
+         dev_err == 0 ? "true" : "false", rank, world, done, dev_err, nccl_version,
+         mode == 1 ? "peer" : mode == -1 ? "nccl" : "undecided");
   return dev_err == 0 ? 0 : 1;
 }
 

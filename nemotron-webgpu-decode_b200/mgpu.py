@@ -125,6 +125,13 @@ class Communicator:
         _lib.check(self.lib.nwd_mgpu_step_times(self.handle, ctypes.byref(a), ctypes.byref(b)))
         return float(a.value), float(b.value)
 
+    def exchange_mode(self) -> str:
+        """"peer" (partials written into every rank's exchange buffer), "nccl"
+        (all-gather + merge) or "undecided" (no step yet)."""
+        v = ctypes.c_int(0)
+        _lib.check(self.lib.nwd_mgpu_exchange_mode(self.handle, ctypes.byref(v)))
+        return {1: "peer", -1: "nccl"}.get(int(v.value), "undecided")
+
     def close(self) -> None:
         if self.handle:
             h, self.handle = self.handle, ctypes.c_void_p()

@@ -35,9 +35,10 @@ def _gpus() -> int:
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-def _child_env():
+def _child_env(exchange: str = "peer"):
     env = dict(os.environ)
     env["NCCL_NVLS_ENABLE"] = "0"  # no NVLink multicast objects bound to a rank that leaves
+    env["NWD_MGPU_P2P"] = "1" if exchange == "peer" else "0"
     return env
 
 
@@ -89,14 +90,14 @@ def _mgpu_ref(oracle, B, L, hq, hkv):
     return np.stack(refs)
 
 
-def _mgpu_ranks(world, tmp_path, extra):
+def _mgpu_ranks(world, tmp_path, extra, exchange="peer"):
     idf = tmp_path / "nccl.id"
     procs = []
     for r in range(world):
         args = [HOST, "mgpu", "--world", str(world), "--rank", str(r), "--device", str(r),
                 "--id-file", str(idf)] + extra
         procs.append(subprocess.Popen(args, stdout=subprocess.PIPE, stderr=subprocess.PIPE,
-                                      text=True, env=_child_env()))
+                                      text=True, env=_child_env(exchange)))
     res = []
     for p in procs:
         try:
@@ -111,28 +112,34 @@ def _mgpu_ranks(world, tmp_path, extra):
     return res
 
 
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
 @pytest.mark.parametrize("world", [1, 2])
-def test_sharded_decode_from_cpp_host(oracle, tmp_path, world):
+def test_sharded_decode_from_cpp_host(oracle, tmp_path, world, exchange):
+    """Both exchanges: partials written into every rank's exchange buffer with a
+    waiting merge (peer), and NCCL all-gather + merge (NWD_MGPU_P2P=0)."""
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")
     B, L, hq, hkv = 2, 65536, 32, 8
     out = tmp_path / "o.bin"
     res = _mgpu_ranks(world, tmp_path, ["--batch", str(B), "--rows", str(L), "--heads", str(hq),
                                         "--kv-heads", str(hkv), "--steps", "3",
-                                        "--out", str(out)])
+                                        "--out", str(out)], exchange)
     for rc, r in res:
         assert rc == 0 and r["ok"], r
+        assert r["exchange"] == exchange, r
     got = f16(np.fromfile(out, np.uint16)).reshape(B, hq, 128)
-    assert_attn_close(got, _mgpu_ref(oracle, B, L, hq, hkv), f"sharded over {world} rank(s)")
+    assert_attn_close(got, _mgpu_ref(oracle, B, L, hq, hkv),
+                      f"sharded over {world} rank(s), {exchange} exchange")
 
 
-def test_rank_leaving_ends_the_next_step_with_an_error(tmp_path):
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
+def test_rank_leaving_ends_the_next_step_with_an_error(tmp_path, exchange):
     if _gpus() < 2:
         pytest.skip("needs 2 GPUs")
     deadline = 2000
     res = _mgpu_ranks(2, tmp_path, ["--batch", "2", "--rows", "32768", "--steps", "3",
                                     "--leave-after", "1", "--step-deadline-ms", str(deadline),
-                                    "--init-deadline-ms", "120000"])
+                                    "--init-deadline-ms", "120000"], exchange)
     (rc0, r0), (rc1, r1) = res
     assert rc1 == 0 and r1.get("left_after") == 1, r1
     assert rc0 == 0 and r0["ok"], r0
@@ -141,8 +148,10 @@ def test_rank_leaving_ends_the_next_step_with_an_error(tmp_path):
     assert r0["after"] == "NWD_OK", r0  # the survivor's context still runs kernels
 
 
-def test_sharded_decode_python_over_the_c_abi(ops, oracle):
-    """mgpu.Communicator (the library's NCCL communicator) at world 1 in this process."""
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
+def test_sharded_decode_python_over_the_c_abi(ops, oracle, monkeypatch, exchange):
+    """mgpu.Communicator (the library's communicator) at world 1 in this process."""
+    monkeypatch.setenv("NWD_MGPU_P2P", "1" if exchange == "peer" else "0")
     mgpu = importlib.import_module(ops.__name__.rsplit(".", 1)[0] + ".mgpu")
     uid = mgpu.share_unique_id(0)
     comm = mgpu.Communicator(uid, 1, 0, torch.cuda.current_device())
@@ -165,8 +174,17 @@ def test_sharded_decode_python_over_the_c_abi(ops, oracle):
                      sl.data_ptr(), o.data_ptr(), B, hq, hkv, 128, wp, nbytes,
                      torch.cuda.current_stream().cuda_stream)
     comm.sync()
+    assert comm.exchange_mode() == exchange
     t_part, t_x = comm.step_times()
     assert t_part > 0 and t_x > 0
+    # later steps reuse the exchange slots by parity: same result, bit for bit
+    first = o.clone()
+    for _ in range(3):
+        comm.decode_step(q.data_ptr(), kp.data_ptr(), vp.data_ptr(), B * L, ro.data_ptr(),
+                         sl.data_ptr(), o.data_ptr(), B, hq, hkv, 128, wp, nbytes,
+                         torch.cuda.current_stream().cuda_stream)
+    comm.sync()
+    assert torch.equal(o, first)
     comm.close()
     qh = oracle.normal_f16(B * hq * 128, 5002).reshape(B, hq, 128)
     for b in range(B):
