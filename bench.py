@@ -15,8 +15,9 @@ across the GPUs, balanced by rows, with no communication (strong scaling;
 
 The same line carries two sub-objects (skipped with ``--no-extras``):
 ``config5``, the long-context step (4 sequences x 1 048 576 rows, each
-sequence's rows sharded over the N GPUs, NCCL all-gather of the partials and
-the merge inside the library), with the exchange's measured share of the step;
+sequence's rows sharded over the N GPUs, the partials exchanged over peer
+memory, or NCCL, and merged inside the library), with the exchange's measured
+share of the step;
 and ``config2``, the single-sequence length sweep on rank 0.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl nwd|reference]
@@ -1173,8 +1174,9 @@ def run_config5(args, ops, torch, dist, dev, rank, world):
 def measure_config5(args, ops, torch, dist, dev, rank, world, sub=False):
     """4 sequences x 1 048 576 rows (Hq=32, Hkv=8), each sequence's
     rows sharded contiguously over the ranks (strong scaling); a step is the shard
-    partial on every GPU, one NCCL all-gather of the packed partials and the LSE
-    merge, run by the library (nwd_mgpu_decode_step) at N > 1, and the partial +
+    partial on every GPU, the exchange of the partials (written into every rank's
+    buffer over peer memory, or one NCCL all-gather) and the LSE merge, run by
+    the library (nwd_mgpu_decode_step) at N > 1, and the partial +
     merge at N = 1.  The K/V data is the same stream whatever the rank count (fill
     offsets follow the global row index), so every N computes the same O.  Returns
     the line (rank 0) or None; with sub=True the figures the config-3 line keeps."""
@@ -1219,19 +1221,14 @@ def measure_config5(args, ops, torch, dist, dev, rank, world, sub=False):
     if sampler:
         sampler.stop()
     ms = a.elapsed_time(e)
-    # where a step's time goes: the shard partial, and the all-gather + merge
+    # where a step's time goes: the shard partial, and the exchange + merge.
+    # One process: events around each.  Several ranks: the exchange's exposed
+    # time is the back-to-back step minus the partial launch alone (timing
+    # single synchronised steps would count the ranks' launch skew as exchange)
     R = min(steps, 20)
-    part_ms, xchg_ms = [], []
-    if sd.comm is not None:
-        sd.comm.set_timing(True)
-        for _ in range(R):
-            sd.step(q, o)
-            sd.sync()
-            pm, xm = sd.comm.step_times()
-            part_ms.append(pm)
-            xchg_ms.append(xm)
-        sd.comm.set_timing(False)
-    else:
+    part_ms, xchg_ms = [0.0], [0.0]
+    if sd.comm is None:
+        part_ms, xchg_ms = [], []
         for _ in range(R):
             e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
             e0.record()
@@ -1277,9 +1274,13 @@ def measure_config5(args, ops, torch, dist, dev, rank, world, sub=False):
     e2.synchronize()
     barrier()
     e2e_ms = a2.elapsed_time(e2)
-    ms_max, e2e_max, _, part_max, xchg_max = max_over_ranks(
+    ms_max, e2e_max, kern_max, part_max, xchg_max = max_over_ranks(
         [ms, e2e_ms, kern_ms, statistics.mean(part_ms), statistics.mean(xchg_ms)], dist, dev)
+    if sd.comm is not None:
+        part_max = kern_max
+        xchg_max = max(0.0, ms_max / steps - kern_max)
     err = sd.workspace.check()
+    exchange = sd.comm.exchange_mode() if sd.comm is not None else "none"
     sd.close()
     del sd
     torch.cuda.empty_cache()
@@ -1296,10 +1297,12 @@ def measure_config5(args, ops, torch, dist, dev, rank, world, sub=False):
             "traffic": (None if traffic5 is None else
                         traffic5 * local_rows / (4.0 * (1 << 20)))}
     split = {"partial_ms": part_max, "exchange_ms": xchg_max,
-             "exchange_share": xchg_max / (part_max + xchg_max),
-             "how": ("CUDA events around the shard partial and around the NCCL all-gather + "
-                     "merge (nwd_mgpu_step_times), one synchronised step at a time, mean of "
-                     f"{R}, max over ranks" if world > 1 else
+             "exchange_share": xchg_max / (part_max + xchg_max), "exchange": exchange,
+             "how": ("the partial: CUDA events around each of "
+                     f"{R} back-to-back shard-partial launches, mean, max over ranks; the "
+                     "exchange + merge: the timed step (max over ranks) minus that, i.e. "
+                     "the part of the step the exchange does not overlap"
+                     if world > 1 else
                      f"CUDA events around the partial and the merge, mean of {R}")}
     value = B * steps / (ms_max * 1e-3)
     if sub:
@@ -1318,9 +1321,9 @@ def measure_config5(args, ops, torch, dist, dev, rank, world, sub=False):
         "hbm_tbs": total_bytes / (ms_max * 1e-3 / steps) / 1e12,
         "config": {"workload": "config5-long-context-split-kv", "sequences": B,
                    "kv_len": L, "heads": HQ, "kv_heads": HKV, "head_dim": HD,
-                   "parallelism": f"rows sharded x{world}, NCCL all-gather of partials "
-                                  "(nwd_mgpu_decode_step)",
-                   "step": "shard partial + all-gather + LSE merge"},
+                   "parallelism": f"rows sharded x{world}, partials exchanged "
+                                  f"({exchange}) by nwd_mgpu_decode_step",
+                   "step": "shard partial + exchange + LSE merge"},
         "roofline": roof, "step_split": split,
         "e2e": {"value": B * steps / (e2e_max * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": B * HQ * HD * 2, "d2h_bytes_per_step": B * HQ * HD * 2},

@@ -96,6 +96,11 @@ struct Params {
   uint32_t cluster;    // > 0: launched as clusters of this many CTAs, one cluster per kv
                        // head (split_k == cluster); the pieces merge over DSMEM
   nwd::XchgDesc x;     // partial mode, x.world > 0: push each pair's partial to every rank
+  // Flattened split of a batch: each non-empty (sequence, kv head) pair of L
+  // rows takes roundup(L + pair_cost, pair_pad) items of the range space
+  // (pair_pad 1, pair_cost 0: L items).
+  uint32_t pair_pad;
+  uint32_t pair_cost;
 };
 
 // ---- shared memory layout (offsets from a 1024-aligned base) ----
@@ -241,6 +246,13 @@ __device__ __forceinline__ uint32_t seq_rows(const Params& p, uint32_t b) {
   if (v <= 0) return 0u;
   return (uint64_t)v > p.pool_rows ? (uint32_t)p.pool_rows : (uint32_t)v;
 }
+// Range items of one (sequence, kv head) pair of L rows, the flattened
+// split's unit: none for an empty pair; for a batch L + pair_cost rounded up
+// to pair_pad, for a single sequence L.
+__device__ __forceinline__ uint32_t pair_items(const Params& p, uint32_t L) {
+  if (L == 0 || !p.seq_len) return L;
+  return (uint32_t)(((uint64_t)L + p.pair_cost + p.pair_pad - 1) / p.pair_pad * p.pair_pad);
+}
 __device__ __forceinline__ int64_t seq_off(const Params& p, uint32_t b) {
   return p.row_offset ? p.row_offset[b] : 0;
 }
@@ -341,11 +353,11 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
   __syncthreads();
   const uint32_t seg = (B + NTHR - 1) / NTHR;
   const uint32_t beg = min(B, tid * seg), end = min(B, beg + seg);
-  uint64_t rows_local = 0;
+  uint64_t rows_local = 0;  // range items of this thread's sequences (one kv head)
   uint32_t max_local = 0;
   for (uint32_t b = beg; b < end; b++) {
     const uint32_t L = seq_rows(p, b);
-    rows_local += L;
+    rows_local += pair_items(p, L);
     max_local = max(max_local, L);
   }
   {
@@ -365,14 +377,14 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
   uint32_t total32;
   uint32_t run = block_scan<NTHR>((uint32_t)rows_local, misc, &total32);  // syncs: sums final
   if (misc->total_rows >= (1ull << 32)) {
-    // more than 2^32 rows in one call: refuse (uniform across the block)
+    // more than 2^32 rows (range items) in one call: refuse (uniform across the block)
     if (early_plan) nwd::pdl_wait();
     if (tid == 0 && blockIdx.x == 0) atomicOr(&wsh->error, NWD_DEVERR_ROW_RANGE);
     return;
   }
   for (uint32_t b = beg; b < end; b++) {
     S[b] = run;
-    run += seq_rows(p, b);
+    run += pair_items(p, seq_rows(p, b));
   }
   if (tid == 0) S[B] = total32;
   __syncthreads();
@@ -388,6 +400,9 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
   const uint64_t T = (uint64_t)p.n_kv * total32;
   uint64_t W = udiv64(T + gridDim.x - 1, gridDim.x);
   if (W < p.min_chunk) W = p.min_chunk;
+  // range ends on a multiple of pair_pad inside every pair: each piece but a
+  // pair's last holds whole stages, an even number of them
+  W = udiv64(W + p.pair_pad - 1, p.pair_pad) * p.pair_pad;
   const uint64_t x0 = min(T, (uint64_t)blockIdx.x * W);
   const uint64_t x1 = min(T, x0 + W);
 
@@ -564,7 +579,7 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
       const uint32_t pair = blockIdx.x / split_k, j = blockIdx.x % split_k;
       if (pair < B * p.n_kv) {
         const uint32_t b = pair / p.n_kv, hkv = pair % p.n_kv;
-        const uint32_t L = S[b + 1] - S[b];
+        const uint32_t L = seq_rows(p, b);
         const uint32_t t0 = (uint32_t)((uint64_t)j * L / split_k);
         const uint32_t t1 = (uint32_t)((uint64_t)(j + 1) * L / split_k);
         PendRow own{}, next{};
@@ -573,35 +588,56 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
                      (int32_t)(pair * split_k + split_k - 1), own, -1, 0u, 0u, next);
       }
     } else if (x0 < x1) {
-      // locate the first piece, then walk pairs forward (no further division
-      // except for the last pair's CTA span)
+      // Locate the first pair, then walk pairs forward.  A pair spans V range
+      // items (pair_items) of which the first L are its rows; a range that
+      // starts or ends in the remaining V - L items has no rows there.
       uint32_t b = find_seq(S, B, udiv64(x0, p.n_kv));
-      uint32_t L = S[b + 1] - S[b];
+      uint32_t V = S[b + 1] - S[b];
+      uint32_t L = seq_rows(p, b);
       const uint64_t r = x0 - (uint64_t)p.n_kv * S[b];
-      uint32_t hkv = (uint32_t)udiv64(r, L);
-      uint32_t t0 = (uint32_t)(r - (uint64_t)hkv * L);
-      uint64_t pstart = x0 - t0;
+      uint32_t hkv = (uint32_t)udiv64(r, V);
+      uint32_t t0 = (uint32_t)(r - (uint64_t)hkv * V);
+      uint64_t pstart = x0 - t0;  // range position of the pair's row 0
+      uint64_t x = x0;
+      // the next pair of the walk (next kv head, or the next non-empty
+      // sequence); only called while the range holds more items, so one exists
+      auto next_pair = [&]() {
+        if (++hkv == p.n_kv) {
+          hkv = 0;
+          do {
+            b++;
+          } while (b + 1 < B && S[b + 1] == S[b]);
+          V = S[b + 1] - S[b];
+          L = seq_rows(p, b);
+        }
+      };
+      if (t0 >= L) {  // the range starts past the pair's rows
+        x = pstart + V;
+        if (x < x1) next_pair();
+        pstart = x;
+        t0 = 0;
+      }
       int32_t f = (int32_t)udiv64(pstart, W);
       PendRow cur{}, nxt{};  // this piece's new row (set up by the piece before), the next one's
-      for (uint64_t x = x0; x < x1 && !aborted;) {
+      while (x < x1 && !aborted) {
         const uint64_t len = min((uint64_t)(L - t0), x1 - x);
         const uint32_t t1 = t0 + (uint32_t)len;
         const bool complete = (t0 == 0 && t1 == L);
         const int32_t l = (t1 == L) ? (int32_t)blockIdx.x : (int32_t)udiv64(pstart + L - 1, W);
         // append mode: the next piece (the next non-empty pair, from its row
-        // 0) ends at its new row if the range holds the whole pair
+        // 0) ends at its new row if the range holds all of its rows
         int32_t nb = -1;
         uint32_t nhkv = 0, nL = 0;
-        if (p.append && x + len < x1) {
-          uint32_t b2 = b, h2 = hkv + 1;
+        if (p.append && pstart + V < x1) {
+          uint32_t b2 = b, h2 = hkv + 1, L2 = L;
           if (h2 == p.n_kv) {
             h2 = 0;
             do {
               b2++;
             } while (b2 + 1 < B && S[b2 + 1] == S[b2]);
+            L2 = seq_rows(p, b2);
           }
-          const uint32_t L2 = S[b2 + 1] - S[b2];
-          if (L2 > 0 && (uint64_t)L2 <= x1 - (x + len)) {
+          if (L2 > 0 && pstart + V + L2 <= x1) {
             nb = (int32_t)b2;
             nhkv = h2;
             nL = L2;
@@ -610,19 +646,14 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
         nxt.valid = nxt.stored = false;
         emit_piece(b, hkv, L, t0, t1, complete, f, l, cur, nb, nhkv, nL, nxt);
         cur = nxt;
-        x += len;
-        if (x >= x1) break;
-        // next pair starts inside this range
+        // the range ends inside the pair's rows, or the pair is done: the
+        // next pair starts V items after this one
+        x = pstart + V;
+        if (t1 < L || x >= x1) break;
+        next_pair();
         pstart = x;
         t0 = 0;
         f = (int32_t)blockIdx.x;
-        if (++hkv == p.n_kv) {
-          hkv = 0;
-          do {
-            b++;
-          } while (b + 1 < B && S[b + 1] == S[b]);
-          L = S[b + 1] - S[b];
-        }
       }
     }
     if (!aborted) {
@@ -1060,6 +1091,16 @@ struct Tuning {
   uint32_t cluster_max = 16;
   uint32_t cluster_rows = 8192;
   uint32_t cluster_keep = 7;
+  // Batches: the flattened split charges each (sequence, kv head) pair its
+  // rows plus pair_cost, rounded up to whole pairs of stages (pair_pad 1), so
+  // every CTA issues the same number of stages and a CTA whose range holds
+  // many pairs takes fewer rows for their fixed costs (first stage, epilogue,
+  // output or partial write).  Config 3 (256 sequences of 512-8 192 rows) per
+  // step: 708 us cut at any row (pair_pad 0: equal rows, up to 4 % more
+  // stages on a CTA holding many pair ends), 702 us padded, 688-691 us with
+  // a cost of 192-384 rows, 697 / 711 us at 512 / 1 024.
+  uint32_t pair_cost = 256;
+  uint32_t pair_pad = 1;
 };
 
 uint32_t env_u32(const char* name, uint32_t dflt) {
@@ -1074,6 +1115,11 @@ const Tuning& tuning() {
     Tuning x;
     x.min_chunk = env_u32("NWD_DECODE_MIN_CHUNK", x.min_chunk);
     x.pair_max = env_u32("NWD_DECODE_PAIR_MAX", x.pair_max);
+    // 0 charges pairs their rows alone
+    const char* pc = getenv("NWD_DECODE_PAIR_COST");
+    if (pc && *pc) x.pair_cost = (uint32_t)std::min<unsigned long>(strtoul(pc, nullptr, 10), 65536ul);
+    const char* pp = getenv("NWD_DECODE_PAIR_PAD");
+    if (pp && *pp) x.pair_pad = strtoul(pp, nullptr, 10) ? 1u : 0u;
     x.groups = env_u32("NWD_DECODE_GROUPS", x.groups);
     if (x.groups > 2) x.groups = 2;
     x.two_group_rows = env_u32("NWD_DECODE_TWO_GROUP_ROWS", x.two_group_rows);
@@ -1370,6 +1416,10 @@ int launch(const Call& c) {
   if (st) return st;
   p.split_k = pl.split_k;
   p.cluster = pl.cluster;
+  // batches: pieces cut at whole pairs of stages (NG stages: one per group),
+  // each pair charged pair_cost items on top of its rows
+  p.pair_pad = c.seq_len && tu.pair_pad ? (uint32_t)TOK * pl.ng : 1u;
+  p.pair_cost = c.seq_len ? tu.pair_cost : 0u;
   const uint32_t grid = pl.grid, ng = pl.ng;
   cudaError_t e;
   if (p.cluster)

@@ -27,20 +27,29 @@ TOK, NST, WPG = 64, 5, 4
 
 # ---------------------------------------------------------------- planner
 
-def plan(lens, nkv, grid, min_chunk=256, pair_max=512, split_k=0):
+def pair_items(L, pad=1, cost=0):
+    """Range items of a (sequence, kv head) pair of L rows: none when empty,
+    else L + cost rounded up to pad (a batch's split; a single sequence runs
+    with pad 1, cost 0)."""
+    return 0 if L == 0 else -(-(L + cost) // pad) * pad
+
+
+def plan(lens, nkv, grid, min_chunk=256, pair_max=512, split_k=0, pad=1, cost=0):
     """Pieces (cta, b, hkv, t0, t1, complete, f, l) as decode_kernel walks them.
 
     split_k > 0: CTA i takes piece i % k of pair i / k (the host's choice for a
     single sequence); otherwise one CTA per pair for small problems, else the
-    flattened equal-range split."""
+    flattened equal-range split over pair_items(L) items per pair, ranges a
+    multiple of pad."""
     B = len(lens)
     S = [0]
     for L in lens:
-        S.append(S[-1] + L)
+        S.append(S[-1] + pair_items(L, pad, cost))
     T = nkv * S[B]
     if split_k == 0 and B * nkv <= grid and max(lens) <= pair_max:
         split_k = 1
     W = max((T + grid - 1) // grid, min_chunk)
+    W = -(-W // pad) * pad
     out = []
     for i in range(grid):
         if split_k:
@@ -56,28 +65,36 @@ def plan(lens, nkv, grid, min_chunk=256, pair_max=512, split_k=0):
         x0, x1 = min(T, i * W), min(T, i * W + W)
         if x0 >= x1:
             continue
-        y = x0 // nkv
-        b = max(j for j in range(B) if S[j] <= y)
-        L = S[b + 1] - S[b]
-        r = x0 - nkv * S[b]
-        h, t0 = divmod(r, L)
-        pstart, f, x = x0 - t0, (x0 - t0) // W, x0
-        while x < x1:
-            ln = min(L - t0, x1 - x)
-            t1 = t0 + ln
-            l = i if t1 == L else (pstart + L - 1) // W
-            out.append((i, b, h, t0, t1, t0 == 0 and t1 == L, f, l))
-            x += ln
-            if x >= x1:
-                break
-            pstart, t0, f = x, 0, i
+        b = max(j for j in range(B) if S[j] <= x0 // nkv)
+        V, L = S[b + 1] - S[b], lens[b]
+        h, t0 = divmod(x0 - nkv * S[b], V)
+        pstart, x = x0 - t0, x0
+
+        def next_pair(b, h):
             h += 1
             if h == nkv:
                 h = 0
                 b += 1
                 while b + 1 < B and S[b + 1] == S[b]:
                     b += 1
-                L = S[b + 1] - S[b]
+            return b, h, S[b + 1] - S[b], lens[b]
+
+        if t0 >= L:  # starts past the pair's rows
+            x = pstart + V
+            if x < x1:
+                b, h, V, L = next_pair(b, h)
+            pstart, t0 = x, 0
+        f = pstart // W
+        while x < x1:
+            ln = min(L - t0, x1 - x)
+            t1 = t0 + ln
+            l = i if t1 == L else (pstart + L - 1) // W
+            out.append((i, b, h, t0, t1, t0 == 0 and t1 == L, f, l))
+            x = pstart + V
+            if t1 < L or x >= x1:
+                break
+            b, h, V, L = next_pair(b, h)
+            pstart, t0, f = x, 0, i
     return out, S
 
 
@@ -85,7 +102,7 @@ def check_plan(lens, nkv, grid, **kw):
     pieces, S = plan(lens, nkv, grid, **kw)
     cover, slots = {}, set()
     for (i, b, h, t0, t1, comp, f, l) in pieces:
-        assert 0 <= t0 < t1 <= S[b + 1] - S[b]
+        assert 0 <= t0 < t1 <= lens[b]
         cover.setdefault((b, h), []).append((t0, t1, i, f, l))
         if not comp:
             s = 2 * i + (0 if t0 > 0 else 1)
@@ -133,9 +150,51 @@ def test_planner_bench_shapes():
     for p in pieces:
         per_cta.setdefault(p[0], 0)
         per_cta[p[0]] += p[4] - p[3]
-    # stream-K: every CTA streams the same rows (the last one the remainder)
+    # unpadded: every CTA streams the same rows (the last one the remainder)
     sizes = sorted(per_cta.values())
     assert sizes[-1] - sizes[1] <= 0
+
+
+def _stages(pieces, ng=2):
+    """Stages each CTA issues: a piece's tiles rounded up to a multiple of ng."""
+    per = {}
+    for (i, b, h, t0, t1, *_r) in pieces:
+        n = -(-(t1 - t0) // TOK)
+        per[i] = per.get(i, 0) + -(-n // ng) * ng
+    return per
+
+
+def test_planner_padded_split_balances_stages_on_config3():
+    """The batch split as the kernel runs it (pairs padded to 2 stages): cut
+    points fall on whole stage pairs, so every CTA but the last issues the same
+    number of stages; unpadded, a CTA whose range holds many pair ends issues
+    up to 4 % more than the mean."""
+    lens = [int(x) for x in np.random.default_rng(3).integers(512, 8193, 256) + 1]
+    flat = _stages(check_plan(lens, 8, 148))
+    padded_pieces = check_plan(lens, 8, 148, pad=2 * TOK)
+    padded = _stages(padded_pieces)
+    assert max(flat.values()) > 1.03 * np.mean(list(flat.values()))
+    W = -(-(8 * sum(pair_items(L, 2 * TOK) for L in lens) // 148) // (2 * TOK)) * 2 * TOK
+    assert all(padded[i] == W // TOK for i in range(147))
+    assert padded[147] <= W // TOK
+    for (i, b, h, t0, t1, *_r) in padded_pieces:
+        assert t0 % (2 * TOK) == 0 and (t1 % (2 * TOK) == 0 or t1 == lens[b])
+
+
+def test_planner_padded_random_shapes():
+    rng = np.random.default_rng(1)
+    for _ in range(300):
+        B = int(rng.integers(1, 120))
+        hi = int(rng.choice([3, 100, 5000, 70000]))
+        lens = [int(x) for x in rng.integers(0, hi, B)]
+        if sum(lens) == 0:
+            continue
+        pad = int(rng.choice([64, 128]))
+        cost = int(rng.choice([0, 64, 200, 1000]))
+        pieces = check_plan(lens, int(rng.choice([1, 2, 8])), int(rng.choice([8, 37, 148])),
+                            min_chunk=int(rng.choice([64, 256])), pad=pad, cost=cost)
+        for (i, b, h, t0, t1, *_r) in pieces:
+            assert t0 % pad == 0 and (t1 % pad == 0 or t1 == lens[b])
 
 
 def prefetch_rows(L, nkv, grid, cta, split_k=0, min_chunk=256, cap=8):
