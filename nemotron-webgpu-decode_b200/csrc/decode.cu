@@ -188,15 +188,17 @@ __device__ __forceinline__ float* xchg_row(const nwd::XchgDesc& x, uint32_t r, u
   const uint32_t par = x.epoch & 1u;
   return x.data[r] + ((size_t)(par * x.world + x.rank) * x.R + row) * nwd::XCH_ROW;
 }
-// Marks pair `pair` of this rank as written on every rank: a system-scope
+// Marks pair `pair` of this rank as written on every rank: one system-scope
 // fence orders the partial's stores (made by this CTA's threads before a
-// barrier) before the flag stores, which release at system scope.
+// barrier) before the flag stores, which are relaxed (fence + relaxed store is
+// a release; a release store per rank would wait on its own fence, world
+// times over NVLink, on the step's critical path).
 __device__ __forceinline__ void xchg_publish(const nwd::XchgDesc& x, uint32_t pair) {
   const uint32_t par = x.epoch & 1u;
   __threadfence_system();
   for (uint32_t r = 0; r < x.world; r++) {
     uint32_t* f = x.flags[r] + (size_t)(par * x.world + x.rank) * x.P + pair;
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(x.epoch) : "memory");
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(f), "r"(x.epoch) : "memory");
   }
 }
 

@@ -49,6 +49,10 @@ __global__ void __launch_bounds__(256) xchg_merge_kernel(const float* __restrict
                                                          uint32_t* dev_err) {
   __shared__ int ok;
   const uint32_t pair = blockIdx.x, par = epoch & 1u;
+  // the next step's partial kernel may take SMs as this step's partial CTAs
+  // leave; it reads nothing before its own griddepcontrol.wait, which returns
+  // once this kernel has completed
+  nwd::pdl_trigger();
   if (threadIdx.x == 0) {
     int good = 1;
     const uint64_t t0 = ptx::globaltimer();
