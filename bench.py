@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Decode-attention bench: tokens/s and achieved HBM bandwidth on B200.
 
-Default workload (the config the metric's 1/2/4/8-GPU
+Default workload (config 3, the configuration the metric's 1/2/4/8-GPU
 scaling is quoted on): 256 independent sequences, Hq=32, Hkv=8, d=128,
 per-sequence KV lengths drawn uniformly from [512, 8192] (seed 3), stored
 contiguously per sequence in one pool, fp16 q/K/V from the deterministic
@@ -459,7 +459,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=30)
     ap.add_argument("--impl", choices=["nwd", "reference"], default="nwd")
     ap.add_argument("--config", choices=["3", "1", "2", "4", "5", "6"], default="3",
-                    help="BASELINE config (6 = the attention layers with their q4 projections)")
+                    help="workload configuration (6 = the attention layers with their q4 projections)")
     ap.add_argument("--scaling", choices=["weak", "strong"], default="strong",
                     help="config 3 at N>1: strong (the 256 sequences split across the GPUs, "
                          "balanced by rows) or weak (256 sequences on every GPU)")
@@ -816,7 +816,7 @@ def small_config_lines(args, ops, torch, dev, which):
 
 
 def run_config4(args, ops, torch, dist, dev, rank, world):
-    """chunked causal prefill, 8 sequences x 2048 prompt tokens per GPU
+    """Config 4: chunked causal prefill, 8 sequences x 2048 prompt tokens per GPU
     (Hq=32, Hkv=8, d=128, scale 1/sqrt(128)).  A step writes the chunk's K/V rows through
     the kv_append path (nwd_kv_append_rows) and runs the tcgen05 prefill attention.
     Sequences shard across GPUs with no communication (weak scaling)."""
@@ -1172,7 +1172,7 @@ def run_config5(args, ops, torch, dist, dev, rank, world):
 
 
 def measure_config5(args, ops, torch, dist, dev, rank, world, sub=False):
-    """4 sequences x 1 048 576 rows (Hq=32, Hkv=8), each sequence's
+    """Config 5: 4 sequences x 1 048 576 rows (Hq=32, Hkv=8), each sequence's
     rows sharded contiguously over the ranks (strong scaling); a step is the shard
     partial on every GPU, the exchange of the partials (written into every rank's
     buffer over peer memory, or one NCCL all-gather) and the LSE merge, run by

@@ -75,7 +75,7 @@ def attention_f64(q, k_pool, v_pool, row_offset, seq_len, n_heads, n_kv, hd, sca
 CASES = {
     # engine shape (engine/config.js:10-12), the last step of the chat-template trace
     "engine_L151": (40, 8, 128, [151], [256], (1, 2, 3)),
-    # BASELINE config 1 as written (group 4), first decode step
+    # config 1 as the benchmark states it (group 4), first decode step
     "g4_L25": (32, 8, 128, [25], [256], (11, 12, 13)),
     # single key: O = V row exactly
     "g4_L1": (32, 8, 128, [1], [8], (21, 22, 23)),

@@ -155,7 +155,7 @@ def test_repeat_calls_identical_and_clean(ops, oracle):
 
 
 def test_engine_trace_config1(engine_mod, oracle):
-    """24 prompt steps + 127 decode steps through the fused step,
+    """Config 1: 24 prompt steps + 127 decode steps through the fused step,
     checked against the oracle at every step (runtime.js:447-467 ordering)."""
     nh, nkv, hd, cap = 40, 8, 128, 256
     layer = engine_mod.DecodeAttention(nh, nkv, hd, cap)
@@ -200,7 +200,7 @@ def test_fused_append_single(ops, oracle, seq):
 
 
 def test_engine_prompt_chunk_then_steps(engine_mod, oracle):
-    """BASELINE config 1 with the 24-token prompt as one chunk (DecodeAttention.prefill,
+    """Config 1 with the 24-token prompt as one chunk (DecodeAttention.prefill,
     the tcgen05 kernel) instead of 24 steps, then 127 decode steps: every output matches
     the reference's token-by-token order (runtime.js:640-646)."""
     nh, nkv, hd, cap, n_prompt = 40, 8, 128, 256, 24

@@ -52,7 +52,7 @@ def test_prefill_vs_oracle(ops, oracle, batch, n_q, start_pos, nh, nkv):
 
 
 def test_prefill_config4_sequence(ops, oracle):
-    """One sequence of BASELINE config 4: 2048 prompt tokens, Hq=32, Hkv=8, causal."""
+    """One sequence of config 4: 2048 prompt tokens, Hq=32, Hkv=8, causal."""
     got, ref = _case(ops, oracle, 1, 2048, 0, 32, 8, seed=4)
     assert_attn_close(got, ref, "2048-token chunk")
 

@@ -1,4 +1,4 @@
-"""Parity tolerance of the attention path.
+"""Parity tolerance of the attention path (the target stated for the port).
 
 fp16 outputs with fp32 accumulation must match the reference restatement to
 max-abs error <= 2e-3 and max-rel error <= 1e-2, where the relative error of
