@@ -93,6 +93,7 @@ struct Params {
   uint32_t pair_max;   // one CTA per (sequence, kv head) when every pair is this short
   uint32_t split_k;    // > 0: CTA i takes piece i % k of pair i / k (k equal pieces per pair)
   uint32_t prefetch;   // single sequence: K/V tiles per CTA prefetched into L2 before the wait
+  uint32_t prefetch_div;  // ... at most 1 / prefetch_div of the CTA's range
   uint32_t cluster;    // > 0: launched as clusters of this many CTAs, one cluster per kv
                        // head (split_k == cluster); the pieces merge over DSMEM
   nwd::XchgDesc x;     // partial mode, x.world > 0: push each pair's partial to every rank
@@ -412,8 +413,8 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
     // A single sequence: start this CTA's first K/V tiles on their way into L2
     // while the previous kernel drains (the rows are read again by TMA after
     // the wait; a row the previous kernel is still writing is updated in L2).
-    // A quarter of the range's tiles, at most p.prefetch: measured on
-    // back-to-back single-sequence steps, prefetching more (or at all for
+    // At most 1 / p.prefetch_div of the range's tiles and p.prefetch: measured
+    // on back-to-back single-sequence steps, prefetching more (or at all for
     // ranges of a few tiles) floods DRAM while the previous kernel's
     // latency-bound merge still runs, and costs more than it hides.
     if (warp == NCW && lane == 0 && !p.row_offset && total32 > 0 && p.prefetch > 0) {
@@ -424,7 +425,7 @@ __global__ void __launch_bounds__(Cfg<NG>::NTHR, 1)
         x = (uint64_t)hkv * L + (uint64_t)j * L / split_k;
         xe = hkv < p.n_kv ? (uint64_t)hkv * L + (uint64_t)(j + 1) * L / split_k : x;
       }
-      uint32_t budget = min(p.prefetch, (uint32_t)(udiv64(xe - x, TOK) / 4u));
+      uint32_t budget = min(p.prefetch, (uint32_t)(udiv64(xe - x, TOK) / p.prefetch_div));
       while (x < xe && budget > 0) {
         const uint32_t hkv = (uint32_t)udiv64(x, L), t = (uint32_t)(x - (uint64_t)hkv * L);
         const uint32_t n = (uint32_t)min((uint64_t)(L - t), xe - x);
@@ -1078,10 +1079,18 @@ struct Tuning {
   uint32_t min_chunk = 256;
   uint32_t pair_max = 512;
   uint32_t groups = 0;  // consumer groups: 0 = by problem size, else 1 or 2
-  uint32_t two_group_rows = 8192;  // single sequence: two groups from this many rows
+  // single sequence: two consumer groups from this many rows (config 2 at
+  // 4 096 rows, clustered: 10.07 us with two groups, 10.32 with one)
+  uint32_t two_group_rows = 4096;
   uint32_t short_rows = 2048;  // single sequence of at most this many rows: decode_short.cu
   uint32_t short_cta_rows = 128;  // past 256 rows: rows per CTA of a kv head's cluster
-  uint32_t prefetch = 8;  // single sequence: K/V tiles per CTA prefetched into L2 under PDL
+  // Single sequence: K/V tiles per CTA prefetched into L2 under PDL, at most
+  // prefetch and 1 / prefetch_div of the CTA's tiles (clustered launches: 8
+  // and a quarter).  Config 2, per step: a quarter / 8 gave 10.30, 17.45 and
+  // 25.28 us at 4 096, 16 384 and 32 768 rows; half / 16 gave 10.39, 17.09
+  // and 25.02 us (4 096 rows runs clustered); all / 32: 10.73, 18.21, 26.93.
+  uint32_t prefetch = 16;
+  uint32_t prefetch_div = 2;
   // single sequence split into k pieces per kv head: run each kv head's pieces
   // as one thread-block cluster (at most cluster_max CTAs, 16 needs the
   // non-portable opt-in) that merges over distributed shared memory; 0 turns
@@ -1133,6 +1142,7 @@ const Tuning& tuning() {
     // 0 turns the prefetch off
     const char* pf = getenv("NWD_DECODE_PREFETCH");
     if (pf && *pf) x.prefetch = (uint32_t)strtoul(pf, nullptr, 10);
+    x.prefetch_div = env_u32("NWD_DECODE_PREFETCH_DIV", x.prefetch_div);
     // 0 turns the cluster merge off
     const char* cl = getenv("NWD_DECODE_CLUSTER");
     if (cl && *cl) x.cluster_max = (uint32_t)strtoul(cl, nullptr, 10);
@@ -1410,7 +1420,7 @@ int launch(const Call& c) {
   p.partial = c.partial ? 1u : 0u;
   if (c.x) p.x = *c.x;  // memset above leaves world = 0 otherwise
   p.min_chunk = tu.min_chunk;
-  p.prefetch = tu.prefetch;
+
   p.pair_max = tu.pair_max;
 
   Plan pl;
@@ -1418,6 +1428,8 @@ int launch(const Call& c) {
   if (st) return st;
   p.split_k = pl.split_k;
   p.cluster = pl.cluster;
+  p.prefetch = pl.cluster ? std::min(tu.prefetch, 8u) : tu.prefetch;
+  p.prefetch_div = pl.cluster ? 4u : tu.prefetch_div;
   // batches: pieces cut at whole pairs of stages (NG stages: one per group),
   // each pair charged pair_cost items on top of its rows
   p.pair_pad = c.seq_len && tu.pair_pad ? (uint32_t)TOK * pl.ng : 1u;

@@ -197,7 +197,7 @@ def test_planner_padded_random_shapes():
             assert t0 % pad == 0 and (t1 % pad == 0 or t1 == lens[b])
 
 
-def prefetch_rows(L, nkv, grid, cta, split_k=0, min_chunk=256, cap=8):
+def prefetch_rows(L, nkv, grid, cta, split_k=0, min_chunk=256, cap=8, div=4):
     """The (kv head, first row) of the K/V tiles CTA `cta` prefetches into L2 before its
     dependency wait, for a single sequence of L rows: csrc/decode.cu's restatement."""
     T = nkv * L
@@ -208,7 +208,7 @@ def prefetch_rows(L, nkv, grid, cta, split_k=0, min_chunk=256, cap=8):
         j, h = cta % split_k, cta // split_k
         x = h * L + j * L // split_k
         xe = h * L + (j + 1) * L // split_k if h < nkv else x
-    budget = min(cap, ((xe - x) // TOK) // 4) if xe > x else 0
+    budget = min(cap, ((xe - x) // TOK) // div) if xe > x else 0
     out = []
     while x < xe and budget > 0:
         h, t = divmod(x, L)
@@ -226,18 +226,19 @@ def prefetch_rows(L, nkv, grid, cta, split_k=0, min_chunk=256, cap=8):
                                    (12000, 1), (9000, 2), (5000, 3)])
 def test_prefetch_stays_inside_the_ctas_pieces(L, nkv):
     """Every tile a CTA prefetches starts on a row its own pieces stream (so the
-    prefetch only moves bytes that CTA reads right after the wait), there are a
-    quarter of its range's whole tiles (at most 8), and they are its first ones."""
-    for split in (True, False):
+    prefetch only moves bytes that CTA reads right after the wait), there are
+    1 / div of its range's whole tiles (at most cap: half and 16 unclustered, a
+    quarter and 8 clustered), and they are its first ones."""
+    for (split, cap, div) in [(s, c, d) for s in (True, False) for c, d in ((16, 2), (8, 4))]:
         grid, k = host_split(L, nkv)
         if not split:
             grid, k = 148, 0
         pieces, _ = plan([L], nkv, grid, split_k=k)
         for cta in range(grid):
             mine = [(h, t0, t1) for (i, b, h, t0, t1, *_rest) in pieces if i == cta]
-            tiles = prefetch_rows(L, nkv, grid, cta, split_k=k)
+            tiles = prefetch_rows(L, nkv, grid, cta, split_k=k, cap=cap, div=div)
             rows = sum(t1 - t0 for _, t0, t1 in mine)
-            assert len(tiles) == min(8, (rows // TOK) // 4)
+            assert len(tiles) == min(cap, (rows // TOK) // div)
             for h, r in tiles:
                 assert any(h == ph and t0 <= r < t1 for ph, t0, t1 in mine)
             # the first tiles of the range, in stream order
