@@ -243,6 +243,16 @@ def step_bytes(L_attended):
     return float(4096 * np.sum(L_attended) + B * (2 * HQ * HD * 2 + 4 * HKV * HD * 2))
 
 
+def hold_stream(torch, steps, host_us_per_step=40.0):
+    """Keep the current stream busy with a bounded spin (torch.cuda._sleep, a
+    fixed number of clock cycles) while the host enqueues `steps` timed
+    launches.  The timed window starts after it, so it measures the GPU running
+    the steps back to back, not Python's launch rate: a 0.1 ms step (config 3
+    on 8 GPUs) otherwise idles whenever the process is descheduled before the
+    host has run ahead of the GPU."""
+    torch.cuda._sleep(int(min(steps * host_us_per_step * 1e-6 * 2.0e9, 4.0e9)))
+
+
 class Config3:
     def __init__(self, ops, torch, rank, world, scaling, dev, batch=None):
         self.ops, self.torch = ops, torch
@@ -530,6 +540,7 @@ def main():
     barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.monotonic()
+    hold_stream(torch, args.steps)
     start.record()
     s_first = s
     for _ in range(args.steps):
@@ -1210,6 +1221,7 @@ def measure_config5(args, ops, torch, dist, dev, rank, world, sub=False):
     barrier()
     t0 = time.monotonic()
     a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    hold_stream(torch, steps)
     a.record()
     for _ in range(steps):
         sd.step(q, o)
