@@ -249,8 +249,10 @@ def hold_stream(torch, steps, host_us_per_step=40.0):
     launches.  The timed window starts after it, so it measures the GPU running
     the steps back to back, not Python's launch rate: a 0.1 ms step (config 3
     on 8 GPUs) otherwise idles whenever the process is descheduled before the
-    host has run ahead of the GPU."""
-    torch.cuda._sleep(int(min(steps * host_us_per_step * 1e-6 * 2.0e9, 4.0e9)))
+    host has run ahead of the GPU.  Skipped if this PyTorch lacks the helper."""
+    sleep = getattr(torch.cuda, "_sleep", None)
+    if sleep is not None:
+        sleep(int(min(steps * host_us_per_step * 1e-6 * 2.0e9, 4.0e9)))
 
 
 class Config3:
